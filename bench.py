@@ -1,0 +1,394 @@
+"""Benchmark of the engine's hot path (BASELINE config 2 by default).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl engine|reference] [--config c2]
+
+One step = one requantized i8 GEMM of BASELINE config 2 (A [4096 x 4096] i8 activations,
+prepacked column-major B [4096 x 4096] i8 weights, per-column i32 bias and f32 scale, zero
+point 0, ReLU, i8 output) through the C ABI (gk_gemm_i8_packed_b_requant_unchecked). Inputs
+are seeded synthetic matrices with the config's distributions; 4 input sets rotate so the
+working set (4 x 48 MiB) exceeds the 126 MB L2. Under torchrun every rank runs its own
+problem (weak scaling, no collective on the data path); the time is the max over ranks.
+
+`--impl reference` times the CPU restatement of gemmkit's multithreaded VNNI path
+(oracle/gk_cpu_baseline.c) on this host's cores for the same metric, on a row sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "int8→i32 GEMM TOPS @4096³ w/ requant (% int8 peak); int8 GEMV HBM GB/s"
+ROTATE = 4
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# ---- clocks ---------------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---- distributed plumbing -------------------------------------------------------------------
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---- workloads --------------------------------------------------------------------------------
+
+class C2:
+    """4096^3 requantized GEMM with a prepacked column-major B."""
+    name = "c2_gemm_i8_requant_4096"
+    m = n = k = 4096
+
+    def __init__(self, seed: int):
+        import torch
+
+        import gemmkit_b200 as gk
+        self.gk = gk
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        m, n, k = self.m, self.n, self.k
+        self.sets = []
+        for _ in range(ROTATE):
+            a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda", generator=g)
+            bT = torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda", generator=g)
+            bias = torch.randint(-2**15, 2**15 + 1, (n,), dtype=torch.int32, device="cuda",
+                                 generator=g)
+            scales = (torch.rand(n, device="cuda", generator=g) * 9e-4 + 1e-4).float()
+            packed = gk.prepack_rhs_i8(gk.MatRef.new(bT.reshape(-1), k, n, 1, k))
+            c = torch.empty(m * n, dtype=torch.int8, device="cuda")
+            req = gk.Requantize(gk.RequantScale.PerCol(scales), 0, bias, gk.AXIS_COL, True)
+            self.sets.append((a, bT, packed, req, c))
+        torch.cuda.synchronize()
+        self.ops = 2.0 * m * n * k
+        self.algo_bytes = m * k + n * k + m * n + 8 * n  # A + B + C + bias + scales
+
+    def step(self, i: int, stream=None):
+        a, _, packed, req, c = self.sets[i % ROTATE]
+        self.gk.gemm_i8_packed_b_requant(self.m, a.data_ptr(), self.k, 1, packed, req,
+                                         c.data_ptr(), 1, self.m, stream=stream)
+
+    launches_per_step = 1
+
+
+class C5:
+    """A [M, 4096] x prepacked B [4096, 14336], per-column scale, i8 out."""
+    k, n = 4096, 14336
+
+    def __init__(self, M: int, seed: int):
+        import torch
+
+        import gemmkit_b200 as gk
+        self.gk, self.M = gk, M
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        self.sets = []
+        for _ in range(ROTATE):
+            a = torch.randint(-127, 128, (M, self.k), dtype=torch.int8, device="cuda", generator=g)
+            bT = torch.randint(-127, 128, (self.n, self.k), dtype=torch.int8, device="cuda",
+                               generator=g)
+            scales = (torch.rand(self.n, device="cuda", generator=g) * 9e-4 + 1e-4).float()
+            packed = gk.prepack_rhs_i8(gk.MatRef.new(bT.reshape(-1), self.k, self.n, 1, self.k))
+            del bT
+            c = torch.empty(M * self.n, dtype=torch.int8, device="cuda")
+            req = gk.Requantize(gk.RequantScale.PerCol(scales), 0)
+            self.sets.append((a, packed, req, c))
+        torch.cuda.synchronize()
+        self.bytes = self.k * self.n + M * self.k + M * self.n + 4 * self.n
+
+    def step(self, i: int, stream=None):
+        a, packed, req, c = self.sets[i % ROTATE]
+        self.gk.gemm_i8_packed_b_requant(self.M, a.data_ptr(), self.k, 1, packed, req,
+                                         c.data_ptr(), self.n, 1, stream=stream)
+
+
+def time_steps(fn, steps: int, warmup: int, ws: int):
+    """CUDA-event time of exactly `steps` calls (after `warmup`), max over ranks, in ms."""
+    import torch
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        fn(warmup + i)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(ws)
+    return max_over_ranks(e0.elapsed_time(e1), ws)
+
+
+def cpu_baseline_c2(budget_s: float = 8.0) -> dict:
+    """Oracle VNNI restatement (all host threads) on a row sample of config 2."""
+    import oracle as O
+    rng = np.random.default_rng(0)
+    k = n = 4096
+    rows = 512
+    a = rng.integers(-127, 128, (rows, k), dtype=np.int8)
+    bT = rng.integers(-127, 128, (n, k), dtype=np.int8)
+    bias = rng.integers(-2**15, 2**15 + 1, n).astype(np.int32)
+    scales = rng.uniform(1e-4, 1e-3, n).astype(np.float32)
+    pb = O.VnniPacked(bT.reshape(-1), 1, k, k, n)
+    c = np.empty(rows * n, np.int8)
+    req = dict(scales=scales, scale_axis="col", bias=bias, bias_axis="col", zp=0, relu=True)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        O.vnni_requant_packed(O.View(a.reshape(-1), rows, k, k, 1), pb,
+                              O.View(c, rows, n, 1, rows), **req)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 50:
+            break
+    med = statistics.median(times)
+    tops = 2.0 * rows * n * k / med / 1e12
+    return {"value": round(tops, 4), "unit": "TOPS", "cores": O.threads(),
+            "kind": "port",
+            "sample": f"{rows} of 4096 rows of config 2 (512x4096x4096, prepacked B, per-col "
+                      f"bias+scale, ReLU), median of {len(times)} runs; C restatement of "
+                      f"gemmkit's AVX-512 VNNI path (vnni={O.has_vnni()})"}
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    import oracle as O
+    rng = np.random.default_rng(0)
+    k = n = 4096
+    rows = 512
+    a = rng.integers(-127, 128, (rows, k), dtype=np.int8)
+    bT = rng.integers(-127, 128, (n, k), dtype=np.int8)
+    bias = rng.integers(-2**15, 2**15 + 1, n).astype(np.int32)
+    scales = rng.uniform(1e-4, 1e-3, n).astype(np.float32)
+    pb = O.VnniPacked(bT.reshape(-1), 1, k, k, n)
+    c = np.empty(rows * n, np.int8)
+    req = dict(scales=scales, scale_axis="col", bias=bias, bias_axis="col", zp=0, relu=True)
+    call = lambda: O.vnni_requant_packed(O.View(a.reshape(-1), rows, k, k, 1), pb,  # noqa: E731
+                                         O.View(c, rows, n, 1, rows), **req)
+    for _ in range(args.warmup):
+        call()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        call()
+    dt = time.perf_counter() - t0
+    ops = 2.0 * rows * n * k * args.steps
+    tops = ops / dt / 1e12
+    sample = (f"{rows} of 4096 rows of config 2 per step (512x4096x4096, prepacked B, per-col "
+              f"bias+scale, ReLU, i8 out); C restatement of gemmkit's multithreaded AVX-512 VNNI "
+              f"path (vnni={O.has_vnni()}); gemmkit itself is Rust and not buildable here")
+    out = {"impl": "reference", "metric": METRIC, "value": round(tops, 4), "unit": "TOPS",
+           "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(dt * 1e3 / args.steps, 4), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic",
+           "config": {"workload": "c2_gemm_i8_requant_4096 (row sample on host cores)",
+                      "m": rows, "n": n, "k": k, "parallelism": "host threads"},
+           "cpu_baseline": {"value": round(tops, 4), "unit": "TOPS", "cores": O.threads(),
+                            "kind": "port", "sample": sample},
+           "e2e": {"value": round(tops, 4), "unit": "TOPS", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-gemv", action="store_true", help="skip the GEMV side measurement")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    ws, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    peaks = load_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+
+    w = C2(seed=1234 + rank)
+    launches_before = w.launches_per_step
+    sampler = ClockSampler(local) if rank == 0 else None
+    for i in range(args.warmup):
+        w.step(i)
+    torch.cuda.synchronize()
+    barrier(ws)
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    ms = time_steps(w.step, args.steps, 0, ws)
+    clocks = sampler.stop() if sampler else None
+    ms_step = ms / args.steps
+    value = ws * w.ops / (ms_step * 1e-3) / 1e12
+
+    # end to end through the public call: pinned host A in, requantized C out, every step
+    a_host = [torch.randint(-127, 128, (w.m * w.k,), dtype=torch.int8).pin_memory()
+              for _ in range(2)]
+    c_host = torch.empty(w.m * w.n, dtype=torch.int8).pin_memory()
+
+    def e2e_step(i):
+        a, _, packed, req, c = w.sets[i % ROTATE]
+        a.view(-1).copy_(a_host[i % 2], non_blocking=True)
+        w.gk.gemm_i8_packed_b_requant(w.m, a.data_ptr(), w.k, 1, packed, req, c.data_ptr(), 1,
+                                      w.m)
+        c_host.copy_(c, non_blocking=True)
+
+    e2e_ms = time_steps(e2e_step, args.e2e_steps, 3, ws) / args.e2e_steps
+    e2e_value = ws * w.ops / (e2e_ms * 1e-3) / 1e12
+
+    gemv = None
+    if not args.no_gemv:
+        gemv = {}
+        for M in (1, 4, 16):
+            g = C5(M, seed=99 + rank)
+            gms = time_steps(g.step, 500, 10, ws) / 500
+            gemv[f"M{M}"] = {"gbs": round(ws * g.bytes / (gms * 1e-3) / 1e9, 1),
+                             "us_per_call": round(gms * 1e3, 2),
+                             "frac_hbm": round(g.bytes / (gms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)}
+            del g
+        torch.cuda.empty_cache()
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        cpu = cpu_baseline_c2()
+
+    if rank == 0:
+        kernel_tops = w.ops / (ms_step * 1e-3) / 1e12
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TOPS", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "i8",
+            "data": "synthetic",
+            "config": {"workload": w.name, "m": w.m, "n": w.n, "k": w.k,
+                       "b": "prepacked, column-major", "c": "column-major i8",
+                       "epilogue": "per-col i32 bias + f32 scale, zp 0, ReLU",
+                       "l2": f"{ROTATE} rotating input sets ({ROTATE * 48} MiB > 126 MB L2)",
+                       "parallelism": f"weak: {ws} independent problems, one per GPU"},
+            "roofline": {"bound": "tensor", "achieved": round(kernel_tops, 2),
+                         "peak": round(int8_peak, 1), "unit": "TOPS",
+                         "frac": round(kernel_tops / int8_peak, 4), "traffic": None,
+                         "peak_source": f"2 x bf16_tflops of {peaks['source']} peaks (B200 dense "
+                                        f"int8 = 2 x dense bf16)",
+                         "kernel": "tc_gemm_kernel<I8,Q8,256>", "algorithmic_ops": w.ops},
+            "e2e": {"value": round(e2e_value, 2), "unit": "TOPS",
+                    "h2d_bytes_per_step": w.m * w.k, "d2h_bytes_per_step": w.m * w.n,
+                    "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": args.steps * launches_before,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "gemv": gemv,
+        }
+        print(json.dumps(out), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

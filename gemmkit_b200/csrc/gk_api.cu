@@ -1,0 +1,979 @@
+// gk_api.cu -- the C ABI (include/gemmkit_cuda.h): gemmkit's validation with its wording,
+// the degenerate-shape rules, the orientation choice, operand packing into the workspace,
+// and the lowering of every entry to one canonical tensor-core problem (gk_engine.h).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+
+#include "gemmkit_cuda.h"
+#include "gk_engine.h"
+
+using gk::AX_M;
+using gk::AX_N;
+using gk::AX_NONE;
+
+struct gk_workspace {
+    int device;
+    void* ptr;
+    size_t cap;
+};
+
+struct gk_packed_rhs {
+    int device;
+    int8_t* buf;  // n rows of kp bytes: B^T, K-contiguous, zero padded
+    size_t k, n, kp;
+};
+
+namespace {
+
+thread_local char g_err[1024] = "";
+thread_local int g_tile_n = -1;
+
+int set_err(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_err(cudaError_t e, const char* what) {
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver ||
+        e == cudaErrorNoKernelImageForDevice)
+        return set_err(GK_ENODEV, "gemmkit: %s: %s", what, cudaGetErrorString(e));
+    if (e == cudaErrorMemoryAllocation)
+        return set_err(GK_ENOMEM, "gemmkit: %s: %s", what, cudaGetErrorString(e));
+    return set_err(GK_ECUDA, "gemmkit: %s: %s", what, cudaGetErrorString(e));
+}
+
+// The engine runs only on sm_100 devices; anything else fails loudly (no fallback).
+int check_device(int* dev_out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_err(e, "no CUDA device");
+    static int ok[64] = {0};
+    if (dev < 0 || dev >= 64) return set_err(GK_ENODEV, "gemmkit: device index out of range");
+    if (ok[dev] == 0) {
+        int major = 0, minor = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+        ok[dev] = (major == 10 && minor == 0) ? 1 : 2;
+    }
+    if (ok[dev] != 1)
+        return set_err(GK_ENODEV, "gemmkit: the CUDA engine needs an sm_100 (B200) device");
+    if (dev_out) *dev_out = dev;
+    return GK_OK;
+}
+
+int tile_n_override() {
+    if (g_tile_n >= 0) return g_tile_n;
+    static int env = -2;
+    if (env == -2) {
+        const char* s = getenv("GEMMKIT_CUDA_BN");
+        int v = s ? atoi(s) : 0;
+        env = (v == 16 || v == 32 || v == 64 || v == 128 || v == 256) ? v : 0;
+    }
+    return env;
+}
+
+// ---- gemmkit's checked-tier validation (gemmkit/src/api.rs:188-315) -----------------------
+
+// extent (gemmkit/src/api.rs:188-210): highest offset (exclusive) reached, or false when a
+// stride paired with a dimension > 1 is negative or the arithmetic overflows.
+bool extent(size_t rows, size_t cols, ptrdiff_t rs, ptrdiff_t cs, size_t* need) {
+    if (rows == 0 || cols == 0) {
+        *need = 0;
+        return true;
+    }
+    __int128 lo = 0, hi = 0;
+    const size_t dims[2] = {rows, cols};
+    const ptrdiff_t strides[2] = {rs, cs};
+    for (int i = 0; i < 2; ++i) {
+        if (dims[i] > static_cast<size_t>(PTRDIFF_MAX)) return false;
+        __int128 e = static_cast<__int128>(dims[i] - 1) * strides[i];
+        if (e > PTRDIFF_MAX || e < PTRDIFF_MIN) return false;
+        if (e < 0)
+            lo += e;
+        else
+            hi += e;
+        if (hi > PTRDIFF_MAX || lo < PTRDIFF_MIN) return false;
+    }
+    if (lo < 0) return false;
+    *need = static_cast<size_t>(hi) + 1;
+    return true;
+}
+
+int check_view(size_t len, size_t rows, size_t cols, ptrdiff_t rs, ptrdiff_t cs, const char* name) {
+    size_t need = 0;
+    if (!extent(rows, cols, rs, cs, &need))
+        return set_err(GK_EINVAL,
+                       "gemmkit: %s view has negative strides or is too large to address; use "
+                       "gemm_unchecked",
+                       name);
+    if (need > len)
+        return set_err(GK_EINVAL,
+                       "gemmkit: %s view of %zux%zu (strides %td,%td) needs %zu elements but slice "
+                       "has %zu",
+                       name, rows, cols, rs, cs, need, len);
+    return GK_OK;
+}
+
+// self_aliases (gemmkit/src/api.rs:236-255)
+bool self_aliases(size_t rows, size_t cols, ptrdiff_t rs, ptrdiff_t cs) {
+    if (rows == 0 || cols == 0) return false;
+    const bool hr = rows > 1, hc = cols > 1;
+    const size_t ars = static_cast<size_t>(rs < 0 ? -rs : rs);
+    const size_t acs = static_cast<size_t>(cs < 0 ? -cs : cs);
+    if (!hr && !hc) return false;
+    if (hr && !hc) return ars == 0;
+    if (!hr && hc) return acs == 0;
+    size_t sm_s, sm_d, big;
+    if (ars <= acs) {
+        sm_s = ars;
+        sm_d = rows;
+        big = acs;
+    } else {
+        sm_s = acs;
+        sm_d = cols;
+        big = ars;
+    }
+    unsigned __int128 span = static_cast<unsigned __int128>(sm_s) * sm_d;
+    return sm_s == 0 || static_cast<unsigned __int128>(big) < span;
+}
+
+// overlaps_bytes (gemmkit/src/api.rs:519-532)
+bool overlaps_bytes(const void* pa, size_t na, size_t sa, const void* pb, size_t nb, size_t sb) {
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(pa), a1 = a0 + na * sa;
+    const uintptr_t b0 = reinterpret_cast<uintptr_t>(pb), b1 = b0 + nb * sb;
+    return a0 < b1 && b0 < a1;
+}
+
+// validate_gemm_views (gemmkit/src/api.rs:270-315)
+int validate_gemm_views(const gk_matref& a, const gk_matref& b, const gk_matmut& c, size_t si,
+                        size_t so) {
+    if (a.cols != b.rows)
+        return set_err(GK_EINVAL, "gemmkit: A.cols (%zu) != B.rows (%zu)", a.cols, b.rows);
+    if (a.rows != c.rows)
+        return set_err(GK_EINVAL, "gemmkit: A.rows (%zu) != C.rows (%zu)", a.rows, c.rows);
+    if (b.cols != c.cols)
+        return set_err(GK_EINVAL, "gemmkit: B.cols (%zu) != C.cols (%zu)", b.cols, c.cols);
+    int rc;
+    if ((rc = check_view(a.len, a.rows, a.cols, a.rs, a.cs, "A"))) return rc;
+    if ((rc = check_view(b.len, b.rows, b.cols, b.rs, b.cs, "B"))) return rc;
+    if ((rc = check_view(c.len, c.rows, c.cols, c.rs, c.cs, "C"))) return rc;
+    if (self_aliases(c.rows, c.cols, c.rs, c.cs))
+        return set_err(GK_EINVAL,
+                       "gemmkit: C view aliases itself (strides %td,%td map distinct elements to "
+                       "the same memory); C must address each (i,j) uniquely",
+                       c.rs, c.cs);
+    if (overlaps_bytes(c.data, c.len, so, a.data, a.len, si) ||
+        overlaps_bytes(c.data, c.len, so, b.data, b.len, si))
+        return set_err(GK_EINVAL, "gemmkit: C aliases A or B");
+    return GK_OK;
+}
+
+// Rust's `{}` formatting of an f32, as the reference's messages print it: shortest
+// round-trip digits, never an exponent, "NaN" / "inf" / "-inf".
+std::string rust_f32(float x) {
+    if (isnan(x)) return "NaN";
+    if (isinf(x)) return x > 0 ? "inf" : "-inf";
+    char buf[64];
+    int prec = 1;
+    for (; prec <= 9; ++prec) {
+        snprintf(buf, sizeof(buf), "%.*e", prec - 1, static_cast<double>(x));
+        if (strtof(buf, nullptr) == x) break;
+    }
+    // buf = d.ddddde[+-]XX; expand to positional notation
+    std::string s(buf);
+    const size_t epos = s.find('e');
+    int exp10 = atoi(s.c_str() + epos + 1);
+    std::string mant = s.substr(0, epos);
+    bool neg = false;
+    if (mant[0] == '-') {
+        neg = true;
+        mant = mant.substr(1);
+    }
+    std::string digits;
+    for (char ch : mant)
+        if (ch != '.') digits.push_back(ch);
+    while (digits.size() > 1 && digits.back() == '0') digits.pop_back();
+    std::string out;
+    const int point = 1 + exp10;  // digits before the decimal point
+    if (point <= 0) {
+        out = "0." + std::string(-point, '0') + digits;
+    } else if (point >= static_cast<int>(digits.size())) {
+        out = digits + std::string(point - digits.size(), '0');
+    } else {
+        out = digits.substr(0, point) + "." + digits.substr(point);
+    }
+    if (out == "0") neg = neg && true;
+    return (neg ? "-" : "") + out;
+}
+
+// ---- workspace -------------------------------------------------------------------------
+
+gk_workspace* default_ws(int dev) {
+    thread_local gk_workspace* tls[64] = {nullptr};
+    if (!tls[dev & 63]) {
+        tls[dev & 63] = new gk_workspace{dev, nullptr, 0};
+    }
+    return tls[dev & 63];
+}
+
+int ws_ensure(gk_workspace* ws, size_t bytes, void** out) {
+    if (bytes == 0) {
+        *out = nullptr;
+        return GK_OK;
+    }
+    if (ws->cap < bytes) {
+        if (ws->ptr) {
+            cudaDeviceSynchronize();  // the old buffer may still be read by queued kernels
+            cudaFree(ws->ptr);
+            ws->ptr = nullptr;
+            ws->cap = 0;
+        }
+        size_t cap = (bytes + (1 << 20) - 1) & ~static_cast<size_t>((1 << 20) - 1);
+        cudaError_t e = cudaMalloc(&ws->ptr, cap);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            ws->ptr = nullptr;
+            return cuda_err(e, "workspace allocation");
+        }
+        ws->cap = cap;
+    }
+    *out = ws->ptr;
+    return GK_OK;
+}
+
+// ---- lowering --------------------------------------------------------------------------
+
+struct Side {  // a user operand view with its batch stride (elements)
+    const void* p;
+    int64_t rs, cs, bs;
+};
+
+struct Job {
+    gk::Kind kind;
+    gk::Out out;
+    int64_t m, k, n, batch;
+    Side a, b;
+    const gk_packed_rhs* packed;
+    void* c;
+    int64_t rsc, csc, cbs;
+    int32_t alpha_i, beta_i;
+    float alpha_f, beta_f;
+    const int32_t* bias;
+    int bias_axis;  // gk_axis (user frame)
+    int64_t bias_bs;
+    const float* scales;
+    int scale_axis;  // gk_axis (user frame)
+    float scale;
+    int64_t scale_bs;
+    int32_t zp, lo, hi;
+    cudaStream_t stream;
+    gk_workspace* ws;
+};
+
+struct KOp {  // an operand in the canonical frame: rows x K, element (r, p) at r*rs + p*ks
+    const void* p;
+    int64_t rows, rs, ks, bs;
+};
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+bool tma_ready(const KOp& o, int64_t K, int64_t batch, int es) {
+    if (o.ks != 1 && K > 1) return false;
+    if (reinterpret_cast<uintptr_t>(o.p) & 15) return false;
+    if (o.rows > 1 && (o.rs <= 0 || (o.rs * es) % 16 != 0 || o.rs < 1)) return false;
+    if (batch > 1 && o.bs != 0 && (o.bs < 0 || (o.bs * es) % 16 != 0)) return false;
+    return true;
+}
+
+int map_axis(int user_axis, bool swap) {
+    if (user_axis == GK_AXIS_ROW) return swap ? AX_N : AX_M;
+    if (user_axis == GK_AXIS_COL) return swap ? AX_M : AX_N;
+    return AX_NONE;
+}
+
+int execute(const Job& j) {
+    if (j.m == 0 || j.n == 0 || j.batch == 0) return GK_OK;
+    int dev = 0;
+    int rc = check_device(&dev);
+    if (rc) return rc;
+    if (j.m > INT32_MAX || j.n > INT32_MAX || j.k > INT32_MAX / 2 || j.batch > INT32_MAX)
+        return set_err(GK_EINVAL, "gemmkit: problem dimensions exceed the engine's limits");
+    const int es = j.kind == gk::Kind::I8 ? 1 : 2;
+    const int eso = j.out == gk::Out::Q8 ? 1 : 4;
+
+    gk::EpiParams e;
+    memset(&e, 0, sizeof(e));
+    e.alpha_i = j.alpha_i;
+    e.beta_i = j.beta_i;
+    e.alpha_f = j.alpha_f;
+    e.beta_f = j.beta_f;
+    e.bias = j.bias;
+    e.bias_bs = j.bias_bs;
+    e.scales = j.scales;
+    e.scale_bs = j.scale_bs;
+    e.scale = j.scale;
+    e.zp = j.zp;
+    e.lo = j.lo;
+    e.hi = j.hi;
+
+    // Degenerate products: gemmkit's scale_c_int (k == 0 or alpha == 0) and
+    // requant_degenerate (k == 0).
+    const bool alpha_zero = (j.out == gk::Out::I32 && j.alpha_i == 0) ||
+                            (j.out == gk::Out::F32 && j.alpha_f == 0.0f);
+    if (j.k == 0 || alpha_zero) {
+        if (j.out == gk::Out::I32) {
+            for (int64_t b = 0; b < j.batch; ++b) {
+                rc = gk::launch_scale_c_i32(static_cast<int32_t*>(j.c) + b * j.cbs, j.m, j.n,
+                                            j.rsc, j.csc, j.beta_i, j.stream);
+                if (rc) return set_err(GK_ECUDA, "gemmkit: fill kernel launch failed");
+            }
+            return GK_OK;
+        }
+        if (j.out == gk::Out::F32) {
+            rc = gk::launch_scale_c_f32(static_cast<float*>(j.c), j.m, j.n, j.rsc, j.csc, j.cbs,
+                                        j.batch, j.beta_f, j.stream);
+            return rc ? set_err(GK_ECUDA, "gemmkit: fill kernel launch failed") : GK_OK;
+        }
+        e.bias_axis = map_axis(j.bias ? j.bias_axis : GK_AXIS_NONE, false);
+        e.scale_axis = map_axis(j.scales ? j.scale_axis : GK_AXIS_NONE, false);
+        rc = gk::launch_requant_fill(j.c, j.m, j.n, j.rsc, j.csc, j.cbs, j.batch, e, j.stream);
+        return rc ? set_err(GK_ECUDA, "gemmkit: fill kernel launch failed") : GK_OK;
+    }
+
+    // Orientation: the output's unit-stride axis becomes the kernel's column axis, except
+    // that a small side (<= 64) always goes to the MMA N so the 128 TMEM lanes stay busy.
+    bool swap;
+    if (j.m <= 64 && j.n > j.m)
+        swap = true;
+    else if (j.n <= 64 && j.m > j.n)
+        swap = false;
+    else if (j.csc == 1)
+        swap = false;
+    else if (j.rsc == 1)
+        swap = true;
+    else
+        swap = llabs(j.csc) > llabs(j.rsc);
+
+    KOp ua{j.a.p, j.m, j.a.rs, j.a.cs, j.a.bs};
+    KOp ub;
+    if (j.packed)
+        ub = KOp{j.packed->buf, j.n, static_cast<int64_t>(j.packed->kp), 1, 0};
+    else
+        ub = KOp{j.b.p, j.n, j.b.cs, j.b.rs, j.b.bs};
+    KOp ka = swap ? ub : ua, kb = swap ? ua : ub;
+    const int64_t Mk = swap ? j.n : j.m, Nk = swap ? j.m : j.n;
+
+    // Operands that are not K-contiguous / 16-byte aligned are packed into the workspace.
+    const int64_t ldp = round_up(j.k, 16 / es);
+    int64_t need[2] = {0, 0};
+    KOp* ops[2] = {&ka, &kb};
+    for (int i = 0; i < 2; ++i) {
+        KOp& o = *ops[i];
+        if (o.rows == 1 && o.ks == 1 && !(reinterpret_cast<uintptr_t>(o.p) & 15)) o.rs = ldp;
+        if (!tma_ready(o, j.k, j.batch, es)) {
+            const int64_t nb = (j.batch > 1 && o.bs != 0) ? j.batch : 1;
+            need[i] = round_up(o.rows * ldp * es * nb, 256);
+        }
+    }
+    if (need[0] || need[1]) {
+        gk_workspace* ws = j.ws ? j.ws : default_ws(dev);
+        void* base = nullptr;
+        rc = ws_ensure(ws, static_cast<size_t>(need[0] + need[1]), &base);
+        if (rc) return rc;
+        char* cur = static_cast<char*>(base);
+        for (int i = 0; i < 2; ++i) {
+            if (!need[i]) continue;
+            KOp& o = *ops[i];
+            const int64_t nb = (j.batch > 1 && o.bs != 0) ? j.batch : 1;
+            const int64_t dbs = o.rows * ldp;
+            if (gk::launch_pack_kmajor(cur, ldp, dbs, o.p, o.rs, o.ks, o.bs, o.rows, j.k, nb, es,
+                                       j.stream))
+                return set_err(GK_ECUDA, "gemmkit: pack kernel launch failed");
+            o = KOp{cur, o.rows, ldp, 1, nb > 1 ? dbs : 0};
+            cur += need[i];
+        }
+    }
+
+    e.out = j.c;
+    e.ldo = swap ? j.csc : j.rsc;
+    e.cso = swap ? j.rsc : j.csc;
+    e.obs = j.cbs;
+    e.bias_axis = map_axis(j.bias ? j.bias_axis : GK_AXIS_NONE, swap);
+    e.scale_axis = map_axis(j.scales ? j.scale_axis : GK_AXIS_NONE, swap);
+    e.vec = (e.cso == 1) && !(reinterpret_cast<uintptr_t>(j.c) & 15) &&
+            ((e.ldo * eso) % 16 == 0 || Mk == 1) && (j.batch <= 1 || (j.cbs * eso) % 16 == 0);
+
+    gk::TcProblem pr;
+    pr.kind = j.kind;
+    pr.out = j.out;
+    pr.Mk = Mk;
+    pr.Nk = Nk;
+    pr.K = j.k;
+    pr.batch = j.batch;
+    pr.a = gk::Operand{ka.p, ka.rows, ka.rs, ka.bs};
+    pr.b = gk::Operand{kb.p, kb.rows, kb.rs, kb.bs};
+    pr.e = e;
+    pr.bn = tile_n_override();
+    pr.stream = j.stream;
+    char err[512] = "";
+    rc = gk::launch_tc_gemm(pr, err, sizeof(err));
+    if (rc) return set_err(rc, "%s", err);
+    return GK_OK;
+}
+
+gk_parallelism par_ignored(gk_parallelism p) { return p; }
+
+// Requant descriptor -> job fields, with the output band of the entry.
+void fill_requant(Job& j, const gk_requant* q, bool out_u8) {
+    j.out = gk::Out::Q8;
+    j.bias = q->bias;
+    j.bias_axis = q->bias ? q->bias_axis : GK_AXIS_NONE;
+    j.scales = q->scale_axis != GK_AXIS_NONE ? q->scales : nullptr;
+    j.scale_axis = q->scale_axis;
+    j.scale = q->scale;
+    j.zp = q->zero_point;
+    j.lo = out_u8 ? 0 : -128;
+    j.hi = out_u8 ? 255 : 127;
+    if (q->relu) {
+        int f = q->zero_point < j.lo ? j.lo : (q->zero_point > j.hi ? j.hi : q->zero_point);
+        if (f > j.lo) j.lo = f;
+    }
+}
+
+Job base_job(gk_workspace* ws, gk_stream_t stream) {
+    Job j;
+    memset(&j, 0, sizeof(j));
+    j.batch = 1;
+    j.ws = ws;
+    j.stream = static_cast<cudaStream_t>(stream);
+    j.alpha_i = 1;
+    j.alpha_f = 1.0f;
+    return j;
+}
+
+int check_scale_value(float s) {
+    if (!(isfinite(s) && s > 0.0f))
+        return set_err(GK_EINVAL, "gemmkit: requantize scale (%s) must be finite and > 0",
+                       rust_f32(s).c_str());
+    return GK_OK;
+}
+
+}  // namespace
+
+// ==========================================================================================
+// C ABI
+// ==========================================================================================
+
+extern "C" {
+
+const char* gk_version(void) { return "gemmkit-cuda 0.1.0 (sm_100a)"; }
+
+const char* gk_last_error(void) { return g_err; }
+
+int gk_device_status(int device, int clear, uint32_t* status) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) return set_err(GK_ENODEV, "gemmkit: bad device");
+    cudaError_t e = cudaDeviceSynchronize();
+    unsigned int* p = gk::device_status_ptr();
+    unsigned int v = 0;
+    if (e == cudaSuccess && p) e = cudaMemcpy(&v, p, sizeof(v), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && clear && p) e = cudaMemset(p, 0, sizeof(v));
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return cuda_err(e, "device status");
+    if (status) *status = v;
+    return GK_OK;
+}
+
+int gk_workspace_create(gk_workspace** out) {
+    if (!out) return set_err(GK_EINVAL, "gemmkit: null output pointer");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    *out = new gk_workspace{dev, nullptr, 0};
+    return GK_OK;
+}
+
+void gk_workspace_free(gk_workspace* ws) {
+    if (!ws) return;
+    if (ws->ptr) {
+        cudaDeviceSynchronize();
+        cudaFree(ws->ptr);
+    }
+    delete ws;
+}
+
+int gk_set_tile_n(int bn) {
+    if (!(bn == 0 || bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 256))
+        return set_err(GK_EINVAL, "gemmkit: tile width must be 0, 16, 32, 64, 128 or 256");
+    g_tile_n = bn;
+    return GK_OK;
+}
+
+// ---- i8 -> i32 ----------------------------------------------------------------------------
+
+int gk_gemm_i8_unchecked(gk_workspace* ws, size_t m, size_t k, size_t n, int32_t alpha,
+                         const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa, const int8_t* b,
+                         ptrdiff_t rsb, ptrdiff_t csb, int32_t beta, int32_t* c, ptrdiff_t rsc,
+                         ptrdiff_t csc, gk_parallelism par, gk_stream_t stream) {
+    (void)par_ignored(par);
+    if (m && n && !c) return set_err(GK_EINVAL, "gemmkit: null C");
+    if (m && n && k && alpha && (!a || !b)) return set_err(GK_EINVAL, "gemmkit: null A or B");
+    Job j = base_job(ws, stream);
+    j.kind = gk::Kind::I8;
+    j.out = gk::Out::I32;
+    j.m = m;
+    j.k = k;
+    j.n = n;
+    j.a = Side{a, rsa, csa, 0};
+    j.b = Side{b, rsb, csb, 0};
+    j.c = c;
+    j.rsc = rsc;
+    j.csc = csc;
+    j.alpha_i = alpha;
+    j.beta_i = beta;
+    return execute(j);
+}
+
+int gk_gemm_i8(gk_workspace* ws, int32_t alpha, gk_matref a, gk_matref b, int32_t beta,
+               gk_matmut c, gk_parallelism par, gk_stream_t stream) {
+    gk_matmut cc = c;
+    int rc = validate_gemm_views(a, b, cc, 1, 4);
+    if (rc) return rc;
+    return gk_gemm_i8_unchecked(ws, a.rows, a.cols, b.cols, alpha,
+                                static_cast<const int8_t*>(a.data), a.rs, a.cs,
+                                static_cast<const int8_t*>(b.data), b.rs, b.cs, beta,
+                                static_cast<int32_t*>(c.data), c.rs, c.cs, par, stream);
+}
+
+// ---- requant ------------------------------------------------------------------------------
+
+int gk_gemm_i8_requant_ex_unchecked(gk_workspace* ws, size_t m, size_t k, size_t n,
+                                    const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa,
+                                    const int8_t* b, ptrdiff_t rsb, ptrdiff_t csb,
+                                    const gk_requant* req, void* c, ptrdiff_t rsc, ptrdiff_t csc,
+                                    int out_u8, gk_parallelism par, gk_stream_t stream) {
+    (void)par_ignored(par);
+    if (!req) return set_err(GK_EINVAL, "gemmkit: null requant descriptor");
+    if (m && n && !c) return set_err(GK_EINVAL, "gemmkit: null C");
+    if (m && n && k && (!a || !b)) return set_err(GK_EINVAL, "gemmkit: null A or B");
+    if (req->scale_axis != GK_AXIS_NONE && !req->scales)
+        return set_err(GK_EINVAL, "gemmkit: null requantize scales");
+    Job j = base_job(ws, stream);
+    j.kind = gk::Kind::I8;
+    j.m = m;
+    j.k = k;
+    j.n = n;
+    j.a = Side{a, rsa, csa, 0};
+    j.b = Side{b, rsb, csb, 0};
+    j.c = c;
+    j.rsc = rsc;
+    j.csc = csc;
+    fill_requant(j, req, out_u8 != 0);
+    return execute(j);
+}
+
+static int requant_plain(gk_workspace* ws, size_t m, size_t k, size_t n, const int8_t* a,
+                         ptrdiff_t rsa, ptrdiff_t csa, const int8_t* b, ptrdiff_t rsb,
+                         ptrdiff_t csb, float scale, const float* row_scales, int has_row_scales,
+                         int32_t zp, const int32_t* bias, int has_bias, void* c, ptrdiff_t rsc,
+                         ptrdiff_t csc, int out_u8, gk_parallelism par, gk_stream_t stream) {
+    gk_requant q;
+    memset(&q, 0, sizeof(q));
+    q.scale = scale;
+    q.scales = has_row_scales ? row_scales : nullptr;
+    q.scale_axis = has_row_scales ? GK_AXIS_ROW : GK_AXIS_NONE;
+    q.zero_point = zp;
+    q.bias = has_bias ? bias : nullptr;
+    q.bias_axis = has_bias ? GK_AXIS_ROW : GK_AXIS_NONE;
+    return gk_gemm_i8_requant_ex_unchecked(ws, m, k, n, a, rsa, csa, b, rsb, csb, &q, c, rsc, csc,
+                                           out_u8, par, stream);
+}
+
+int gk_gemm_i8_requant_unchecked(gk_workspace* ws, size_t m, size_t k, size_t n, const int8_t* a,
+                                 ptrdiff_t rsa, ptrdiff_t csa, const int8_t* b, ptrdiff_t rsb,
+                                 ptrdiff_t csb, float scale, const float* row_scales,
+                                 int has_row_scales, int32_t zero_point, const int32_t* bias,
+                                 int has_bias, int8_t* c, ptrdiff_t rsc, ptrdiff_t csc,
+                                 gk_parallelism par, gk_stream_t stream) {
+    return requant_plain(ws, m, k, n, a, rsa, csa, b, rsb, csb, scale, row_scales, has_row_scales,
+                         zero_point, bias, has_bias, c, rsc, csc, 0, par, stream);
+}
+
+int gk_gemm_i8_requant_u8_unchecked(gk_workspace* ws, size_t m, size_t k, size_t n,
+                                    const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa,
+                                    const int8_t* b, ptrdiff_t rsb, ptrdiff_t csb, float scale,
+                                    const float* row_scales, int has_row_scales,
+                                    int32_t zero_point, const int32_t* bias, int has_bias,
+                                    uint8_t* c, ptrdiff_t rsc, ptrdiff_t csc, gk_parallelism par,
+                                    gk_stream_t stream) {
+    return requant_plain(ws, m, k, n, a, rsa, csa, b, rsb, csb, scale, row_scales, has_row_scales,
+                         zero_point, bias, has_bias, c, rsc, csc, 1, par, stream);
+}
+
+// requant_scale / requant_bias (gemmkit/src/adapter.rs:190-280) over C's backing slice as a
+// unit-stride footprint, in gemmkit's order: views, scale, zero-point, bias.
+static int validate_requant(const gk_requant* q, size_t m, size_t n, const gk_matmut& c,
+                            int out_u8, cudaStream_t st) {
+    const size_t c_bytes = c.len;  // 1-byte output
+    auto axis_len = [&](int axis) { return axis == GK_AXIS_COL ? n : m; };
+    const char* axis_dim = nullptr;
+    if (q->scale_axis == GK_AXIS_NONE) {
+        int rc = check_scale_value(q->scale);
+        if (rc) return rc;
+    } else {
+        const size_t want = axis_len(q->scale_axis);
+        axis_dim = q->scale_axis == GK_AXIS_COL ? "B.cols" : "A.rows";
+        if (q->scales_len != want)
+            return set_err(GK_EINVAL, "gemmkit: requantize scales length (%zu) != %s (%zu)",
+                           q->scales_len, axis_dim, want);
+        if (c_bytes && q->scales_len &&
+            overlaps_bytes(c.data, c_bytes, 1, q->scales, q->scales_len, 4))
+            return set_err(GK_EINVAL, "gemmkit: requantize scales overlap C");
+        if (q->scales_len) {
+            float* host = static_cast<float*>(malloc(q->scales_len * sizeof(float)));
+            if (!host) return set_err(GK_ENOMEM, "gemmkit: host allocation failed");
+            cudaError_t e = cudaMemcpyAsync(host, q->scales, q->scales_len * sizeof(float),
+                                            cudaMemcpyDeviceToHost, st);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+            if (e != cudaSuccess) {
+                free(host);
+                return cuda_err(e, "reading requantize scales");
+            }
+            for (size_t i = 0; i < q->scales_len; ++i) {
+                int rc = check_scale_value(host[i]);
+                if (rc) {
+                    free(host);
+                    return rc;
+                }
+            }
+            free(host);
+        }
+    }
+    if (out_u8) {
+        if (q->zero_point < 0 || q->zero_point > 255)
+            return set_err(GK_EINVAL,
+                           "gemmkit: requantize zero_point (%d) out of u8 range [0, 255]",
+                           q->zero_point);
+    } else if (q->zero_point < -128 || q->zero_point > 127) {
+        return set_err(GK_EINVAL, "gemmkit: requantize zero_point (%d) out of i8 range [-128, 127]",
+                       q->zero_point);
+    }
+    if (q->bias) {
+        const size_t want = axis_len(q->bias_axis);
+        const char* dim = q->bias_axis == GK_AXIS_COL ? "B.cols" : "A.rows";
+        if (q->bias_len != want)
+            return set_err(GK_EINVAL, "gemmkit: requantize bias length (%zu) != %s (%zu)",
+                           q->bias_len, dim, want);
+        if (c_bytes && q->bias_len && overlaps_bytes(c.data, c_bytes, 1, q->bias, q->bias_len, 4))
+            return set_err(GK_EINVAL, "gemmkit: requantize bias overlaps C");
+    }
+    return GK_OK;
+}
+
+int gk_gemm_i8_requant(gk_workspace* ws, gk_matref a, gk_matref b, const gk_requant* req,
+                       gk_matmut c, int out_u8, gk_parallelism par, gk_stream_t stream) {
+    if (!req) return set_err(GK_EINVAL, "gemmkit: null requant descriptor");
+    int rc = validate_gemm_views(a, b, c, 1, 1);
+    if (rc) return rc;
+    rc = validate_requant(req, a.rows, b.cols, c, out_u8, static_cast<cudaStream_t>(stream));
+    if (rc) return rc;
+    return gk_gemm_i8_requant_ex_unchecked(
+        ws, a.rows, a.cols, b.cols, static_cast<const int8_t*>(a.data), a.rs, a.cs,
+        static_cast<const int8_t*>(b.data), b.rs, b.cs, req, c.data, c.rs, c.cs, out_u8, par,
+        stream);
+}
+
+// ---- prepacked B --------------------------------------------------------------------------
+
+int gk_prepack_rhs_i8_unchecked(const int8_t* b, ptrdiff_t rsb, ptrdiff_t csb, size_t k, size_t n,
+                                gk_stream_t stream, gk_packed_rhs** out) {
+    if (!out) return set_err(GK_EINVAL, "gemmkit: null output pointer");
+    *out = nullptr;
+    int dev = 0;
+    int rc = check_device(&dev);
+    if (rc) return rc;
+    if (k > static_cast<size_t>(INT32_MAX / 2) || n > static_cast<size_t>(INT32_MAX))
+        return set_err(GK_EINVAL,
+                       "gemmkit: prepacked RHS of %zux%zu is too large; the pack buffer size "
+                       "overflows usize",
+                       k, n);
+    gk_packed_rhs* p = new gk_packed_rhs{dev, nullptr, k, n, 0};
+    p->kp = static_cast<size_t>(round_up(static_cast<int64_t>(k), 16));
+    const size_t bytes = p->kp * n;
+    if (bytes) {
+        if (!b) {
+            delete p;
+            return set_err(GK_EINVAL, "gemmkit: null B");
+        }
+        cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&p->buf), bytes);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            delete p;
+            return cuda_err(e, "prepack allocation");
+        }
+        // B^T rows (one per column j of B): element (j, p) = b[p*rsb + j*csb]
+        if (gk::launch_pack_kmajor(p->buf, p->kp, 0, b, csb, rsb, 0, n, k, 1, 1,
+                                   static_cast<cudaStream_t>(stream))) {
+            cudaFree(p->buf);
+            delete p;
+            return set_err(GK_ECUDA, "gemmkit: pack kernel launch failed");
+        }
+    }
+    *out = p;
+    return GK_OK;
+}
+
+int gk_prepack_rhs_i8(gk_matref b, gk_stream_t stream, gk_packed_rhs** out) {
+    int rc = check_view(b.len, b.rows, b.cols, b.rs, b.cs, "B");
+    if (rc) return rc;
+    return gk_prepack_rhs_i8_unchecked(static_cast<const int8_t*>(b.data), b.rs, b.cs, b.rows,
+                                       b.cols, stream, out);
+}
+
+void gk_packed_rhs_free(gk_packed_rhs* p) {
+    if (!p) return;
+    if (p->buf) {
+        cudaDeviceSynchronize();
+        cudaFree(p->buf);
+    }
+    delete p;
+}
+
+size_t gk_packed_rhs_rows(const gk_packed_rhs* p) { return p ? p->k : 0; }
+size_t gk_packed_rhs_cols(const gk_packed_rhs* p) { return p ? p->n : 0; }
+
+int gk_gemm_i8_packed_b_unchecked(gk_workspace* ws, int32_t alpha, size_t m, const int8_t* a,
+                                  ptrdiff_t rsa, ptrdiff_t csa, const gk_packed_rhs* packed,
+                                  int32_t beta, int32_t* c, ptrdiff_t rsc, ptrdiff_t csc,
+                                  gk_parallelism par, gk_stream_t stream) {
+    (void)par_ignored(par);
+    if (!packed) return set_err(GK_EINVAL, "gemmkit: null packed RHS");
+    // gemmkit/src/api/packed.rs:626-631
+    if (llabs(csc) < llabs(rsc))
+        return set_err(GK_EINVAL,
+                       "gemmkit: gemm_packed_b requires column-major-ish C (|csc| >= |rsc|); a "
+                       "row-major C would swap A/B and invalidate the prepacked RHS \xe2\x80\x94 "
+                       "use gemm() for that layout");
+    if (m && packed->n && !c) return set_err(GK_EINVAL, "gemmkit: null C");
+    if (m && packed->n && packed->k && alpha && !a) return set_err(GK_EINVAL, "gemmkit: null A");
+    Job j = base_job(ws, stream);
+    j.kind = gk::Kind::I8;
+    j.out = gk::Out::I32;
+    j.m = m;
+    j.k = packed->k;
+    j.n = packed->n;
+    j.a = Side{a, rsa, csa, 0};
+    j.packed = packed;
+    j.c = c;
+    j.rsc = rsc;
+    j.csc = csc;
+    j.alpha_i = alpha;
+    j.beta_i = beta;
+    return execute(j);
+}
+
+int gk_gemm_i8_packed_b(gk_workspace* ws, int32_t alpha, gk_matref a, const gk_packed_rhs* packed,
+                        int32_t beta, gk_matmut c, gk_parallelism par, gk_stream_t stream) {
+    if (!packed) return set_err(GK_EINVAL, "gemmkit: null packed RHS");
+    // gemmkit/src/api/packed.rs:503-553
+    if (a.cols != packed->k)
+        return set_err(GK_EINVAL, "gemmkit: A.cols (%zu) != packed B.rows (%zu)", a.cols,
+                       packed->k);
+    if (packed->n != c.cols)
+        return set_err(GK_EINVAL, "gemmkit: packed B.cols (%zu) != C.cols (%zu)", packed->n,
+                       c.cols);
+    if (a.rows != c.rows)
+        return set_err(GK_EINVAL, "gemmkit: A.rows (%zu) != C.rows (%zu)", a.rows, c.rows);
+    int rc;
+    if ((rc = check_view(a.len, a.rows, a.cols, a.rs, a.cs, "A"))) return rc;
+    if ((rc = check_view(c.len, c.rows, c.cols, c.rs, c.cs, "C"))) return rc;
+    if (self_aliases(c.rows, c.cols, c.rs, c.cs))
+        return set_err(GK_EINVAL,
+                       "gemmkit: C view aliases itself (strides %td,%td map distinct elements to "
+                       "the same memory); C must address each (i,j) uniquely",
+                       c.rs, c.cs);
+    if (overlaps_bytes(c.data, c.len, 4, a.data, a.len, 1))
+        return set_err(GK_EINVAL, "gemmkit: C aliases A");
+    return gk_gemm_i8_packed_b_unchecked(ws, alpha, a.rows, static_cast<const int8_t*>(a.data),
+                                         a.rs, a.cs, packed, beta, static_cast<int32_t*>(c.data),
+                                         c.rs, c.cs, par, stream);
+}
+
+int gk_gemm_i8_packed_b_requant_unchecked(gk_workspace* ws, size_t m, const int8_t* a,
+                                          ptrdiff_t rsa, ptrdiff_t csa,
+                                          const gk_packed_rhs* packed, const gk_requant* req,
+                                          void* c, ptrdiff_t rsc, ptrdiff_t csc, int out_u8,
+                                          gk_parallelism par, gk_stream_t stream) {
+    (void)par_ignored(par);
+    if (!packed) return set_err(GK_EINVAL, "gemmkit: null packed RHS");
+    if (!req) return set_err(GK_EINVAL, "gemmkit: null requant descriptor");
+    if (m && packed->n && !c) return set_err(GK_EINVAL, "gemmkit: null C");
+    if (m && packed->n && packed->k && !a) return set_err(GK_EINVAL, "gemmkit: null A");
+    if (req->scale_axis != GK_AXIS_NONE && !req->scales)
+        return set_err(GK_EINVAL, "gemmkit: null requantize scales");
+    Job j = base_job(ws, stream);
+    j.kind = gk::Kind::I8;
+    j.m = m;
+    j.k = packed->k;
+    j.n = packed->n;
+    j.a = Side{a, rsa, csa, 0};
+    j.packed = packed;
+    j.c = c;
+    j.rsc = rsc;
+    j.csc = csc;
+    fill_requant(j, req, out_u8 != 0);
+    return execute(j);
+}
+
+// ---- batched ------------------------------------------------------------------------------
+
+int gk_gemm_i8_requant_batched_unchecked(gk_workspace* ws, size_t batch, size_t m, size_t k,
+                                         size_t n, const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa,
+                                         ptrdiff_t a_bs, const int8_t* b, ptrdiff_t rsb,
+                                         ptrdiff_t csb, ptrdiff_t b_bs, const gk_requant* req,
+                                         ptrdiff_t bias_bs, ptrdiff_t scales_bs, void* c,
+                                         ptrdiff_t rsc, ptrdiff_t csc, ptrdiff_t c_bs, int out_u8,
+                                         gk_parallelism par, gk_stream_t stream) {
+    (void)par_ignored(par);
+    if (!req) return set_err(GK_EINVAL, "gemmkit: null requant descriptor");
+    if (batch && m && n && !c) return set_err(GK_EINVAL, "gemmkit: null C");
+    if (batch && m && n && k && (!a || !b)) return set_err(GK_EINVAL, "gemmkit: null A or B");
+    if (req->scale_axis != GK_AXIS_NONE && !req->scales)
+        return set_err(GK_EINVAL, "gemmkit: null requantize scales");
+    Job j = base_job(ws, stream);
+    j.kind = gk::Kind::I8;
+    j.m = m;
+    j.k = k;
+    j.n = n;
+    j.batch = batch;
+    j.a = Side{a, rsa, csa, a_bs};
+    j.b = Side{b, rsb, csb, b_bs};
+    j.c = c;
+    j.rsc = rsc;
+    j.csc = csc;
+    j.cbs = c_bs;
+    fill_requant(j, req, out_u8 != 0);
+    j.bias_bs = bias_bs;
+    j.scale_bs = scales_bs;
+    if (batch > 1 && c_bs == 0 && m && n)
+        return set_err(GK_EINVAL, "gemmkit: batched C elements must not alias (c_bs == 0)");
+    return execute(j);
+}
+
+int gk_gemm_i8_requant_batched_ptr_unchecked(gk_workspace* ws,
+                                             const gk_i8_requant_problem* problems, size_t count,
+                                             int out_u8, gk_parallelism par, gk_stream_t stream) {
+    if (count && !problems) return set_err(GK_EINVAL, "gemmkit: null problem list");
+    for (size_t i = 0; i < count; ++i) {
+        const gk_i8_requant_problem& p = problems[i];
+        int rc = gk_gemm_i8_requant_ex_unchecked(ws, p.m, p.k, p.n, p.a, p.rsa, p.csa, p.b, p.rsb,
+                                                 p.csb, &p.req, p.c, p.rsc, p.csc, out_u8, par,
+                                                 stream);
+        if (rc) return rc;
+    }
+    return GK_OK;
+}
+
+// ---- half -> f32 ---------------------------------------------------------------------------
+
+static int half_f32(gk_workspace* ws, bool f16, size_t batch, size_t m, size_t k, size_t n,
+                    float alpha, const uint16_t* a, ptrdiff_t rsa, ptrdiff_t csa, ptrdiff_t a_bs,
+                    const uint16_t* b, ptrdiff_t rsb, ptrdiff_t csb, ptrdiff_t b_bs, float beta,
+                    float* c, ptrdiff_t rsc, ptrdiff_t csc, ptrdiff_t c_bs, gk_stream_t stream) {
+    if (batch && m && n && !c) return set_err(GK_EINVAL, "gemmkit: null C");
+    if (batch && m && n && k && alpha != 0.0f && (!a || !b))
+        return set_err(GK_EINVAL, "gemmkit: null A or B");
+    Job j = base_job(ws, stream);
+    j.kind = f16 ? gk::Kind::F16 : gk::Kind::BF16;
+    j.out = gk::Out::F32;
+    j.m = m;
+    j.k = k;
+    j.n = n;
+    j.batch = batch;
+    j.a = Side{a, rsa, csa, a_bs};
+    j.b = Side{b, rsb, csb, b_bs};
+    j.c = c;
+    j.rsc = rsc;
+    j.csc = csc;
+    j.cbs = c_bs;
+    j.alpha_f = alpha;
+    j.beta_f = beta;
+    if (batch > 1 && c_bs == 0 && m && n)
+        return set_err(GK_EINVAL, "gemmkit: batched C elements must not alias (c_bs == 0)");
+    return execute(j);
+}
+
+int gk_gemm_bf16_f32_unchecked(gk_workspace* ws, size_t m, size_t k, size_t n, float alpha,
+                               const uint16_t* a, ptrdiff_t rsa, ptrdiff_t csa, const uint16_t* b,
+                               ptrdiff_t rsb, ptrdiff_t csb, float beta, float* c, ptrdiff_t rsc,
+                               ptrdiff_t csc, gk_parallelism par, gk_stream_t stream) {
+    (void)par_ignored(par);
+    return half_f32(ws, false, 1, m, k, n, alpha, a, rsa, csa, 0, b, rsb, csb, 0, beta, c, rsc,
+                    csc, 0, stream);
+}
+
+int gk_gemm_f16_f32_unchecked(gk_workspace* ws, size_t m, size_t k, size_t n, float alpha,
+                              const uint16_t* a, ptrdiff_t rsa, ptrdiff_t csa, const uint16_t* b,
+                              ptrdiff_t rsb, ptrdiff_t csb, float beta, float* c, ptrdiff_t rsc,
+                              ptrdiff_t csc, gk_parallelism par, gk_stream_t stream) {
+    (void)par_ignored(par);
+    return half_f32(ws, true, 1, m, k, n, alpha, a, rsa, csa, 0, b, rsb, csb, 0, beta, c, rsc,
+                    csc, 0, stream);
+}
+
+int gk_gemm_half_f32(gk_workspace* ws, int is_f16, float alpha, gk_matref a, gk_matref b,
+                     float beta, gk_matmut c, gk_parallelism par, gk_stream_t stream) {
+    int rc = validate_gemm_views(a, b, c, 2, 4);
+    if (rc) return rc;
+    (void)par_ignored(par);
+    return half_f32(ws, is_f16 != 0, 1, a.rows, a.cols, b.cols, alpha,
+                    static_cast<const uint16_t*>(a.data), a.rs, a.cs, 0,
+                    static_cast<const uint16_t*>(b.data), b.rs, b.cs, 0, beta,
+                    static_cast<float*>(c.data), c.rs, c.cs, 0, stream);
+}
+
+int gk_gemm_half_f32_batched_unchecked(gk_workspace* ws, int is_f16, size_t batch, size_t m,
+                                       size_t k, size_t n, float alpha, const uint16_t* a,
+                                       ptrdiff_t rsa, ptrdiff_t csa, ptrdiff_t a_bs,
+                                       const uint16_t* b, ptrdiff_t rsb, ptrdiff_t csb,
+                                       ptrdiff_t b_bs, float beta, float* c, ptrdiff_t rsc,
+                                       ptrdiff_t csc, ptrdiff_t c_bs, gk_parallelism par,
+                                       gk_stream_t stream) {
+    (void)par_ignored(par);
+    return half_f32(ws, is_f16 != 0, batch, m, k, n, alpha, a, rsa, csa, a_bs, b, rsb, csb, b_bs,
+                    beta, c, rsc, csc, c_bs, stream);
+}
+
+// ---- self test -----------------------------------------------------------------------------
+
+int gk_selftest_wait_timeout(uint64_t timeout_ns, gk_stream_t stream) {
+    int dev = 0;
+    int rc = check_device(&dev);
+    if (rc) return rc;
+    uint32_t before = 0;
+    rc = gk_device_status(dev, 1, &before);
+    if (rc) return rc;
+    if (gk::launch_selftest_timeout(timeout_ns, static_cast<cudaStream_t>(stream)))
+        return set_err(GK_ECUDA, "gemmkit: self-test launch failed");
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_err(e, "self-test");
+    uint32_t st = 0;
+    rc = gk_device_status(dev, 1, &st);
+    if (rc) return rc;
+    if (st & 0x10u)
+        return set_err(GK_ETIMEOUT, "gemmkit: device wait gave up after %llu ns (status 0x%x)",
+                       static_cast<unsigned long long>(timeout_ns), st);
+    return GK_OK;
+}
+
+}  // extern "C"

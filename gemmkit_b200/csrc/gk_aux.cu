@@ -1,0 +1,176 @@
+// gk_aux.cu -- the engine's memory-bound helper kernels:
+//   * pack_kmajor: gather any strided (even negative-stride) operand into the K-contiguous,
+//     16-byte-aligned rows the TMA loads need (gemmkit's pack step, gemmkit/src/pack.rs,
+//     re-targeted at the tensor-core tile layout); a 32 x 32 shared-memory tile keeps both
+//     the read and the write side coalesced whichever of the source strides is 1;
+//   * the degenerate fills of gemmkit's k == 0 / alpha == 0 paths
+//     (gemmkit/src/dispatch/int.rs:150-163 scale_c_int, :735-752 requant_degenerate);
+//   * the bounded-wait self test.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gk_engine.h"
+#include "gk_sm100.cuh"
+
+namespace gk {
+
+template <typename T>
+__global__ void pack_kmajor_kernel(T* __restrict__ dst, int64_t dld, int64_t dbs,
+                                   const T* __restrict__ src, int64_t srs, int64_t scs,
+                                   int64_t sbs, int64_t rows, int64_t K) {
+    __shared__ T tile[32][33];
+    const int64_t e = blockIdx.z;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32;
+    const int64_t k0 = static_cast<int64_t>(blockIdx.x) * 32;
+    const T* s = src + e * sbs;
+    T* d = dst + e * dbs;
+    const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+    const bool k_fast = (scs == 1) || (srs != 1 && scs <= srs);
+    // read: consecutive threads walk the source's unit-stride axis
+    for (int i = ty; i < 32; i += 8) {
+        int64_t r, k;
+        if (k_fast) {
+            r = r0 + i;
+            k = k0 + tx;
+        } else {
+            r = r0 + tx;
+            k = k0 + i;
+        }
+        T v = T(0);
+        if (r < rows && k < K) v = s[r * srs + k * scs];
+        if (k_fast)
+            tile[i][tx] = v;
+        else
+            tile[tx][i] = v;
+    }
+    __syncthreads();
+    // write: consecutive threads walk K (row-major destination), zero in the K padding
+    for (int i = ty; i < 32; i += 8) {
+        const int64_t r = r0 + i, k = k0 + tx;
+        if (r < rows && k < dld) d[r * dld + k] = tile[i][tx];
+    }
+}
+
+int launch_pack_kmajor(void* dst, int64_t dld, int64_t dbs, const void* src, int64_t srs,
+                       int64_t scs, int64_t sbs, int64_t rows, int64_t K, int64_t batch, int es,
+                       cudaStream_t st) {
+    if (rows == 0 || dld == 0 || batch == 0) return 0;
+    dim3 block(32, 8);
+    dim3 grid(static_cast<unsigned>((dld + 31) / 32), static_cast<unsigned>((rows + 31) / 32),
+              static_cast<unsigned>(batch));
+    if (grid.y > 65535u || grid.z > 65535u) return 1;
+    if (es == 1)
+        pack_kmajor_kernel<int8_t><<<grid, block, 0, st>>>(
+            static_cast<int8_t*>(dst), dld, dbs, static_cast<const int8_t*>(src), srs, scs, sbs,
+            rows, K);
+    else
+        pack_kmajor_kernel<uint16_t><<<grid, block, 0, st>>>(
+            static_cast<uint16_t*>(dst), dld, dbs, static_cast<const uint16_t*>(src), srs, scs,
+            sbs, rows, K);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+__global__ void scale_c_i32_kernel(int32_t* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,
+                                   int32_t beta) {
+    const int64_t total = m * n;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t j = idx / m, i = idx - j * m;
+        int32_t* p = c + i * rsc + j * csc;
+        if (beta == 0)
+            *p = 0;
+        else
+            *p = static_cast<int32_t>(static_cast<uint32_t>(beta) * static_cast<uint32_t>(*p));
+    }
+}
+
+int launch_scale_c_i32(int32_t* c, int64_t m, int64_t n, int64_t rsc, int64_t csc, int32_t beta,
+                       cudaStream_t st) {
+    if (m == 0 || n == 0 || beta == 1) return 0;
+    int64_t blocks = (m * n + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    scale_c_i32_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(c, m, n, rsc, csc, beta);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+__global__ void scale_c_f32_kernel(float* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,
+                                   int64_t cbs, int64_t batch, float beta) {
+    const int64_t per = m * n, total = per * batch;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t e = idx / per, r = idx - e * per;
+        const int64_t j = r / m, i = r - j * m;
+        float* p = c + e * cbs + i * rsc + j * csc;
+        *p = beta == 0.0f ? 0.0f : beta * *p;
+    }
+}
+
+int launch_scale_c_f32(float* c, int64_t m, int64_t n, int64_t rsc, int64_t csc, int64_t cbs,
+                       int64_t batch, float beta, cudaStream_t st) {
+    if (m == 0 || n == 0 || batch == 0 || beta == 1.0f) return 0;
+    int64_t blocks = (m * n * batch + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    scale_c_f32_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(c, m, n, rsc, csc, cbs,
+                                                                      batch, beta);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+// k == 0: every element is KRequantize::apply(0, i, j), computed with the reference's own
+// sequence in f64 (this path is not hot).
+__global__ void requant_fill_kernel(uint8_t* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,
+                                    int64_t cbs, int64_t batch, EpiParams e) {
+    const int64_t per = m * n, total = per * batch;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t b = idx / per, r = idx - b * per;
+        const int64_t j = r / m, i = r - j * m;
+        int32_t bias = 0;
+        if (e.bias_axis == AX_M) bias = e.bias[b * e.bias_bs + i];
+        if (e.bias_axis == AX_N) bias = e.bias[b * e.bias_bs + j];
+        float s = e.scale;
+        if (e.scale_axis == AX_M) s = e.scales[b * e.scale_bs + i];
+        if (e.scale_axis == AX_N) s = e.scales[b * e.scale_bs + j];
+        const double x = __dmul_rn(static_cast<double>(bias), static_cast<double>(s));
+        // round half to even, saturating like `as i64` (|x| stays below 2^31 * 3.4e38)
+        long long qv = __double2ll_rn(x);
+        if (qv > (1LL << 40)) qv = 1LL << 40;
+        if (qv < -(1LL << 40)) qv = -(1LL << 40);
+        long long q = qv + e.zp;
+        if (q < e.lo) q = e.lo;
+        if (q > e.hi) q = e.hi;
+        c[b * cbs + i * rsc + j * csc] = static_cast<uint8_t>(q);
+    }
+}
+
+int launch_requant_fill(void* c, int64_t m, int64_t n, int64_t rsc, int64_t csc, int64_t cbs,
+                        int64_t batch, const EpiParams& e, cudaStream_t st) {
+    if (m == 0 || n == 0 || batch == 0) return 0;
+    int64_t blocks = (m * n * batch + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    requant_fill_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+        static_cast<uint8_t*>(c), m, n, rsc, csc, cbs, batch, e);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+// Waits on an mbarrier that nothing arrives on; the bounded wait gives up after timeout_ns,
+// records GK_DEV_TIMEOUT_SELFTEST and the kernel returns normally.
+__global__ void selftest_timeout_kernel(uint64_t timeout_ns, unsigned int* status) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+        mbar_wait(&bar, 0, &abort_flag, status, GK_DEV_TIMEOUT_SELFTEST, timeout_ns);
+    __syncthreads();
+}
+
+int launch_selftest_timeout(uint64_t timeout_ns, cudaStream_t st) {
+    selftest_timeout_kernel<<<1, 32, 0, st>>>(timeout_ns, device_status_ptr());
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+}  // namespace gk

@@ -1,0 +1,202 @@
+"""C-ABI checks that need no GPU: the library loads, exports every entry the header declares,
+validates like gemmkit (same messages), and fails loudly (GK_ENODEV) instead of falling back
+when there is no sm_100 device."""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+import gemmkit_b200 as gk
+from gemmkit_b200 import _build, _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gemmkit_cuda.h")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def built():
+    _build.build()
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(gk_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_exports_every_declared_symbol():
+    lib = C.CDLL(_lib.lib_path())
+    syms = declared_symbols()
+    assert len(syms) >= 25
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+    # and the Python binding declares a signature for every one of them
+    assert set(syms) <= set(_lib.SIGNATURES), set(syms) - set(_lib.SIGNATURES)
+
+
+def test_version():
+    assert b"sm_100a" in _lib.load().gk_version()
+
+
+def host(n, dtype=np.int8):
+    arr = np.zeros(n, dtype)
+    return (arr.ctypes.data, n), arr
+
+
+def expect_err(fn, substr, code=gk.GK_EINVAL):
+    with pytest.raises(gk.GemmkitError) as ei:
+        fn()
+    assert substr in str(ei.value), str(ei.value)
+    assert ei.value.code == code
+
+
+def test_shape_mismatch_messages():
+    (pa, _), ka = host(16)
+    (pb, _), kb = host(16)
+    (pc, _), kc = host(16, np.int32)
+    a = gk.MatRef((pa, 16), 4, 4, 4, 1)
+    b = gk.MatRef((pb, 16), 3, 4, 4, 1)
+    c = gk.MatMut((pc, 16), 4, 4, 4, 1)
+    expect_err(lambda: gk.gemm_i8(1, a, b, 0, c), "gemmkit: A.cols (4) != B.rows (3)")
+    b = gk.MatRef((pb, 16), 4, 4, 4, 1)
+    c2 = gk.MatMut((pc, 16), 3, 4, 4, 1)
+    expect_err(lambda: gk.gemm_i8(1, a, b, 0, c2), "gemmkit: A.rows (4) != C.rows (3)")
+    c3 = gk.MatMut((pc, 16), 4, 3, 4, 1)
+    expect_err(lambda: gk.gemm_i8(1, a, b, 0, c3), "gemmkit: B.cols (4) != C.cols (3)")
+
+
+def test_view_bounds_and_alias_messages():
+    (pa, _), ka = host(16)
+    (pb, _), kb = host(16)
+    (pc, _), kc = host(16, np.int32)
+    a_short = gk.MatRef((pa, 15), 4, 4, 4, 1)
+    b = gk.MatRef((pb, 16), 4, 4, 4, 1)
+    c = gk.MatMut((pc, 16), 4, 4, 4, 1)
+    expect_err(lambda: gk.gemm_i8(1, a_short, b, 0, c),
+               "gemmkit: A view of 4x4 (strides 4,1) needs 16 elements but slice has 15")
+    a_neg = gk.MatRef((pa, 16), 4, 4, -4, 1)
+    expect_err(lambda: gk.gemm_i8(1, a_neg, b, 0, c),
+               "gemmkit: A view has negative strides or is too large to address; use gemm_unchecked")
+    a = gk.MatRef((pa, 16), 4, 4, 4, 1)
+    c_alias = gk.MatMut((pc, 16), 4, 4, 0, 1)
+    expect_err(lambda: gk.gemm_i8(1, a, b, 0, c_alias), "C view aliases itself (strides 0,1")
+    # C overlapping A (byte ranges), as gemmkit's validate_gemm_views
+    c_over = gk.MatMut((pa, 4), 2, 2, 2, 1)
+    a2 = gk.MatRef((pa, 16), 2, 8, 8, 1)
+    b2 = gk.MatRef((pb, 16), 8, 2, 2, 1)
+    expect_err(lambda: gk.gemm_i8(1, a2, b2, 0, c_over), "gemmkit: C aliases A or B")
+
+
+def requant_call(scale=gk.RequantScale.PerTensor(0.5), zp=0, bias=None, u8=False):
+    (pa, _), ka = host(16)
+    (pb, _), kb = host(16)
+    (pc, _), kc = host(16, np.int8)
+    a = gk.MatRef((pa, 16), 4, 4, 4, 1)
+    b = gk.MatRef((pb, 16), 4, 4, 4, 1)
+    c = gk.MatMut((pc, 16), 4, 4, 4, 1)
+    req = gk.Requantize(scale, zp, bias)
+    fn = gk.gemm_i8_requant_u8 if u8 else gk.gemm_i8_requant
+    return lambda: fn(a, b, req, c, sync=False), (ka, kb, kc)
+
+
+@pytest.mark.parametrize("bad", [0.0, -1.0, float("nan"), float("inf")])
+def test_requant_bad_scale(bad):
+    """gemmkit/tests/epilogue/requant.rs:578 (expected = "scale")."""
+    fn, keep = requant_call(scale=gk.RequantScale.PerTensor(bad))
+    want = {0.0: "(0)", -1.0: "(-1)"}.get(bad, "")
+    expect_err(fn, f"gemmkit: requantize scale {want}".rstrip() if want else "must be finite and > 0")
+
+
+def test_requant_bad_zp():
+    """requant.rs:599 / :1053 / :1074 (expected = "zero_point")."""
+    fn, keep = requant_call(zp=128)
+    expect_err(fn, "gemmkit: requantize zero_point (128) out of i8 range [-128, 127]")
+    fn, keep = requant_call(zp=-129)
+    expect_err(fn, "zero_point (-129) out of i8 range")
+    fn, keep = requant_call(zp=256, u8=True)
+    expect_err(fn, "gemmkit: requantize zero_point (256) out of u8 range [0, 255]")
+    fn, keep = requant_call(zp=-1, u8=True)
+    expect_err(fn, "zero_point (-1) out of u8 range")
+
+
+def test_requant_bad_bias_len_and_overlap():
+    """requant.rs:620 / :1095 (expected = "bias length")."""
+    bias = np.zeros(3, np.int32)
+    fn, keep = requant_call(bias=(bias.ctypes.data, 3))
+    expect_err(fn, "gemmkit: requantize bias length (3) != A.rows (4)")
+    (pa, _), ka = host(16)
+    (pb, _), kb = host(16)
+    cbuf = np.zeros(64, np.int8)
+    a = gk.MatRef((pa, 16), 4, 4, 4, 1)
+    b = gk.MatRef((pb, 16), 4, 4, 4, 1)
+    c = gk.MatMut((cbuf.ctypes.data, 16), 4, 4, 4, 1)
+    req = gk.Requantize(gk.RequantScale.PerTensor(1.0), 0, (cbuf.ctypes.data + 4, 4))
+    expect_err(lambda: gk.gemm_i8_requant(a, b, req, c, sync=False),
+               "gemmkit: requantize bias overlaps C")
+
+
+def test_requant_per_row_scale_len_and_overlap():
+    """requant.rs:1461 (expected = "scales length"), :1527 ("scales overlap C")."""
+    s = np.ones(3, np.float32)
+    fn, keep = requant_call(scale=gk.RequantScale.PerRow((s.ctypes.data, 3)))
+    expect_err(fn, "gemmkit: requantize scales length (3) != A.rows (4)")
+    (pa, _), ka = host(16)
+    (pb, _), kb = host(16)
+    cbuf = np.zeros(64, np.int8)
+    a = gk.MatRef((pa, 16), 4, 4, 4, 1)
+    b = gk.MatRef((pb, 16), 4, 4, 4, 1)
+    c = gk.MatMut((cbuf.ctypes.data, 16), 4, 4, 4, 1)
+    req = gk.Requantize(gk.RequantScale.PerRow((cbuf.ctypes.data + 8, 4)), 0)
+    expect_err(lambda: gk.gemm_i8_requant(a, b, req, c, sync=False),
+               "gemmkit: requantize scales overlap C")
+
+
+def test_packed_b_requires_colmajor_c():
+    lib = _lib.load()
+    rc = lib.gk_gemm_i8_packed_b_unchecked(None, 1, 4, 0, 4, 1, C.c_void_p(1), 0, 0, 4, 1,
+                                           _lib.Parallelism(0, 0), None)
+    assert rc == gk.GK_EINVAL
+    assert "requires column-major-ish C (|csc| >= |rsc|)" in _lib.last_error()
+
+
+def test_rust_float_formatting_in_messages():
+    for v, txt in [(1e-30, "0.000000000000000000000000000001"), (-2.5, "-2.5"),
+                   (float("-inf"), "-inf"), (0.0, "0")]:
+        fn, keep = requant_call(scale=gk.RequantScale.PerTensor(v))
+        if v > 0:
+            continue
+        expect_err(fn, f"gemmkit: requantize scale ({txt}) must be finite and > 0")
+
+
+def test_valid_call_without_gpu_fails_loudly():
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present")
+    except ImportError:
+        pass
+    (pa, _), ka = host(16)
+    (pb, _), kb = host(16)
+    (pc, _), kc = host(16, np.int32)
+    a = gk.MatRef((pa, 16), 4, 4, 4, 1)
+    b = gk.MatRef((pb, 16), 4, 4, 4, 1)
+    c = gk.MatMut((pc, 16), 4, 4, 4, 1)
+    with pytest.raises(gk.GemmkitError) as ei:
+        gk.gemm_i8(1, a, b, 0, c, sync=False)
+    assert ei.value.code in (gk.GK_ENODEV,), str(ei.value)
+    assert kc.sum() == 0  # nothing computed on the host
+
+
+def test_empty_problem_is_noop_without_device():
+    lib = _lib.load()
+    rc = lib.gk_gemm_i8_unchecked(None, 0, 5, 5, 1, None, 0, 0, None, 0, 0, 0, None, 0, 0,
+                                  _lib.Parallelism(0, 0), None)
+    assert rc == gk.GK_OK
+
+
+def test_set_tile_n_validation():
+    gk.set_tile_n(0)
+    with pytest.raises(gk.GemmkitError):
+        gk.set_tile_n(48)

@@ -1,0 +1,120 @@
+"""GPU accuracy of the bf16 / f16 -> f32 path through the C ABI: within 1e-2 relative of an
+f64 reference dot (the stated tolerance), and the reference tests' own relative Frobenius
+gate 8*k*eps (gemmkit/tests/oracle_common/mod.rs:185-219)."""
+import numpy as np
+import pytest
+
+import gemmkit_b200 as gk
+import oracle as O
+from gpu_util import dev, empty, gather, host
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-2  # per element, relative to alpha*sum|a||b| + |beta*c| (the dot's magnitude)
+EPS = {False: 2.0 ** -8, True: 2.0 ** -11}  # bf16 / f16 unit roundoff
+
+
+@pytest.fixture(autouse=True)
+def _reset_tile():
+    gk.set_tile_n(0)
+    yield
+    gk.set_tile_n(0)
+    assert gk.device_status(0) == 0
+
+
+def f16_bits(x):
+    return np.asarray(x, np.float32).astype(np.float16).view(np.uint16)
+
+
+def widen(bits, is_f16):
+    return (bits.view(np.float16).astype(np.float64) if is_f16
+            else O.bf16_to_f32(bits).astype(np.float64))
+
+
+def make(rng, shape, is_f16):
+    x = rng.standard_normal(shape).astype(np.float32)
+    return f16_bits(x) if is_f16 else O.f32_to_bf16(x)
+
+
+def check(got, a, b, alpha, beta, c0, is_f16, rows=None):
+    rows = np.arange(a.shape[0]) if rows is None else rows
+    ref = O.gemm_half_f64(a[rows], b, alpha, beta, None if c0 is None else c0[rows], is_f16)
+    mag = abs(alpha) * (np.abs(widen(a[rows], is_f16)) @ np.abs(widen(b, is_f16)))
+    if c0 is not None:
+        mag += abs(beta) * np.abs(c0[rows].astype(np.float64))
+    err = np.abs(got[rows].astype(np.float64) - ref)
+    assert np.all(err <= REL_TOL * mag + 1e-30), float((err / (mag + 1e-30)).max())
+    k = a.shape[1]
+    fro = np.linalg.norm(got[rows] - ref) / max(np.linalg.norm(ref), 1e-30)
+    assert fro <= 8 * k * EPS[is_f16], fro
+
+
+@pytest.mark.parametrize("is_f16", [False, True])
+@pytest.mark.parametrize("shape", [(128, 64, 256), (200, 333, 129), (1, 4096, 999), (517, 8, 61),
+                                   (64, 1000, 16)])
+@pytest.mark.parametrize("alpha,beta", [(1.0, 0.0), (1.0, 0.5), (-2.0, 1.0)])
+def test_half_f32_shapes(is_f16, shape, alpha, beta):
+    m, k, n = shape
+    rng = np.random.default_rng(m * 31 + k * 7 + n)
+    a = make(rng, (m, k), is_f16)
+    b = make(rng, (k, n), is_f16)
+    c0 = rng.standard_normal((m, n)).astype(np.float32)
+    da, db = dev(a.view(np.int16)), dev(b.view(np.int16))
+    dc = dev(c0)
+    gk.gemm_half_f32(alpha, gk.MatRef.from_row_major(da, m, k), gk.MatRef.from_row_major(db, k, n),
+                     beta, gk.MatMut.from_row_major(dc, m, n), is_f16=is_f16)
+    check(host(dc).reshape(m, n), a, b, alpha, beta, c0 if beta else None, is_f16)
+
+
+@pytest.mark.parametrize("layout", ["rc", "cr", "cc"])
+def test_half_layouts(layout):
+    rng = np.random.default_rng(5)
+    m, k, n = 150, 270, 190
+    a = make(rng, (m, k), False)
+    b = make(rng, (k, n), False)
+    abuf = a.reshape(-1) if layout[0] == "r" else np.ascontiguousarray(a.T).reshape(-1)
+    rsa, csa = (k, 1) if layout[0] == "r" else (1, m)
+    bbuf = b.reshape(-1) if layout[1] == "r" else np.ascontiguousarray(b.T).reshape(-1)
+    rsb, csb = (n, 1) if layout[1] == "r" else (1, k)
+    dc = empty(m * n, np.float32)
+    gk.gemm_half_f32(1.0, gk.MatRef.new(dev(abuf.view(np.int16)), m, k, rsa, csa),
+                     gk.MatRef.new(dev(bbuf.view(np.int16)), k, n, rsb, csb), 0.0,
+                     gk.MatMut.from_col_major(dc, m, n))
+    got = gather(host(dc), m, n, 1, m)
+    check(got, a, b, 1.0, 0.0, None, False)
+
+
+def test_c3_config_full_size_sampled():
+    """8192^3 bf16 N(0,1), C f32 N(0,1), alpha 1, beta 0.5."""
+    rng = np.random.default_rng(3)
+    m = n = k = 8192
+    a = O.f32_to_bf16(rng.standard_normal((m, k), dtype=np.float32))
+    b = O.f32_to_bf16(rng.standard_normal((k, n), dtype=np.float32))
+    c0 = rng.standard_normal((m, n), dtype=np.float32)
+    da, db, dc = dev(a.view(np.int16)), dev(b.view(np.int16)), dev(c0)
+    gk.gemm_half_f32(1.0, gk.MatRef.from_row_major(da, m, k), gk.MatRef.from_row_major(db, k, n),
+                     0.5, gk.MatMut.from_row_major(dc, m, n))
+    got = host(dc).reshape(m, n)
+    rows = np.sort(rng.choice(m, 12, replace=False))
+    check(got, a, b, 1.0, 0.5, c0, False, rows=rows)
+    assert np.isfinite(got).all()
+
+
+def test_half_batched():
+    rng = np.random.default_rng(8)
+    batch, m, k, n = 5, 96, 200, 144
+    a = make(rng, (batch, m, k), False)
+    b = make(rng, (batch, k, n), False)
+    da, db = dev(a.view(np.int16)), dev(b.view(np.int16))
+    dc = empty(batch * m * n, np.float32)
+    gk.gemm_half_f32_batched(False, batch, m, k, n, 1.0, da.data_ptr(), k, 1, m * k, db.data_ptr(),
+                             n, 1, k * n, 0.0, dc.data_ptr(), n, 1, m * n)
+    got = host(dc).reshape(batch, m, n)
+    for e in range(batch):
+        check(got[e], a[e], b[e], 1.0, 0.0, None, False)
+
+
+def test_half_degenerate():
+    dc = dev(np.arange(6, dtype=np.float32))
+    gk.gemm_bf16_f32_unchecked(2, 0, 3, 1.0, 0, 0, 1, 0, 3, 1, 2.0, dc.data_ptr(), 3, 1)
+    assert host(dc).tolist() == [0.0, 2.0, 4.0, 6.0, 8.0, 10.0]
