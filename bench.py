@@ -197,6 +197,137 @@ class C5:
                                          c.data_ptr(), self.n, 1, stream=stream)
 
 
+class C1:
+    """M=N=K=1024 i8 -> i32, row-major A and B, alpha 1, beta 0."""
+    name = "c1_gemm_i8_i32_1024"
+    m = n = k = 1024
+    unit, bound = "TOPS", "tensor"
+
+    def __init__(self, seed: int):
+        import torch
+
+        import gemmkit_b200 as gk
+        self.gk = gk
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        self.sets = []
+        for _ in range(16):  # 16 x 6 MiB rotating sets > L2
+            a = torch.randint(-128, 128, (self.m * self.k,), dtype=torch.int8, device="cuda",
+                              generator=g)
+            b = torch.randint(-128, 128, (self.k * self.n,), dtype=torch.int8, device="cuda",
+                              generator=g)
+            c = torch.zeros(self.m * self.n, dtype=torch.int32, device="cuda")
+            self.sets.append((a, b, c))
+        self.work = 2.0 * self.m * self.n * self.k
+        self.bytes = self.m * self.k + self.k * self.n + 4 * self.m * self.n
+
+    def step(self, i: int, stream=None):
+        a, b, c = self.sets[i % len(self.sets)]
+        self.gk.gemm_i8_unchecked(self.m, self.k, self.n, 1, a.data_ptr(), self.k, 1,
+                                  b.data_ptr(), self.n, 1, 0, c.data_ptr(), self.n, 1,
+                                  stream=stream)
+
+
+class C3:
+    """8192^3 bf16 x bf16 -> f32, A/B N(0,1), C N(0,1), alpha 1, beta 0.5."""
+    name = "c3_gemm_bf16_f32_8192"
+    m = n = k = 8192
+    unit, bound = "TFLOP/s", "tensor"
+
+    def __init__(self, seed: int):
+        import torch
+
+        import gemmkit_b200 as gk
+        self.gk = gk
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        m, n, k = self.m, self.n, self.k
+        self.a = torch.randn(m * k, device="cuda", generator=g).to(torch.bfloat16)
+        self.bT = torch.randn(n * k, device="cuda", generator=g).to(torch.bfloat16)
+        self.c = torch.randn(m * n, device="cuda", generator=g)
+        self.work = 2.0 * m * n * k
+        self.bytes = 2 * (m * k + n * k) + 8 * m * n
+
+    def step(self, i: int, stream=None):
+        self.gk.gemm_bf16_f32_unchecked(self.m, self.k, self.n, 1.0, self.a.data_ptr(), self.k, 1,
+                                        self.bT.data_ptr(), 1, self.k, 0.5, self.c.data_ptr(),
+                                        self.n, 1, stream=stream)
+
+
+class C4:
+    """512 x (512x512x128) i8, per-row bias, per-col scale, u8 zp 128."""
+    name = "c4_batched_i8_requant_u8"
+    batch, m, n, k = 512, 512, 512, 128
+    unit, bound = "GB/s", "hbm"
+
+    def __init__(self, seed: int):
+        import torch
+
+        import gemmkit_b200 as gk
+        self.gk = gk
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        B, m, n, k = self.batch, self.m, self.n, self.k
+        self.a = torch.randint(-128, 128, (B * m * k,), dtype=torch.int8, device="cuda", generator=g)
+        self.bT = torch.randint(-128, 128, (B * n * k,), dtype=torch.int8, device="cuda",
+                                generator=g)
+        self.bias = torch.randint(-2**15, 2**15 + 1, (B * m,), dtype=torch.int32, device="cuda",
+                                  generator=g)
+        self.scales = (torch.rand(B * n, device="cuda", generator=g) * 9e-4 + 1e-4).float()
+        self.c = torch.empty(B * m * n, dtype=torch.uint8, device="cuda")
+        self.req = gk.Requantize(gk.RequantScale.PerCol(self.scales), 128, self.bias, gk.AXIS_ROW)
+        self.work = 2.0 * B * m * n * k
+        self.bytes = B * (m * k + n * k + m * n + 4 * m + 4 * n)
+
+    def step(self, i: int, stream=None):
+        B, m, n, k = self.batch, self.m, self.n, self.k
+        self.gk.gemm_i8_requant_batched(B, m, k, n, self.a.data_ptr(), k, 1, m * k,
+                                        self.bT.data_ptr(), 1, k, n * k, self.req, m, n,
+                                        self.c.data_ptr(), 1, m, m * n, out_u8=True, stream=stream)
+
+
+class C5M(C5):
+    unit, bound = "GB/s", "hbm"
+
+    def __init__(self, M: int, seed: int):
+        super().__init__(M, seed)
+        self.name = f"c5_gemv_i8_requant_M{M}"
+        self.work = 2.0 * M * self.k * self.n
+
+
+def run_config(args, ws, rank, local):
+    """One BASELINE config on its own (its own metric); used for profiles and ncu."""
+    import torch
+    torch.cuda.set_device(local)
+    peaks = load_peaks()
+    cfg = args.config
+    if cfg == "c1":
+        w = C1(7 + rank)
+    elif cfg == "c3":
+        w = C3(7 + rank)
+    elif cfg == "c4":
+        w = C4(7 + rank)
+    elif cfg.startswith("c5"):
+        w = C5M(int(cfg[2:] or 16) if cfg != "c5" else 16, 7 + rank)
+    else:
+        w = C2(7 + rank)
+        w.unit, w.bound, w.work, w.bytes = "TOPS", "tensor", w.ops, w.algo_bytes
+    ms = time_steps(w.step, args.steps, args.warmup, ws) / args.steps
+    if w.unit == "GB/s":
+        val = ws * w.bytes / (ms * 1e-3) / 1e9
+        peak, kval = peaks["hbm_gbs"], w.bytes / (ms * 1e-3) / 1e9
+    else:
+        val = ws * w.work / (ms * 1e-3) / 1e12
+        kval = w.work / (ms * 1e-3) / 1e12
+        peak = peaks["bf16_tflops"] * (2.0 if w.unit == "TOPS" else 1.0)
+    if rank == 0:
+        print(json.dumps({"config": cfg, "workload": w.name, "value": round(val, 2),
+                          "unit": w.unit, "ms_per_step": round(ms, 5), "n_gpus": ws,
+                          "steps": args.steps, "warmup": args.warmup,
+                          "tops_or_tflops": round(ws * w.work / (ms * 1e-3) / 1e12, 2),
+                          "gbs": round(ws * w.bytes / (ms * 1e-3) / 1e9, 1),
+                          "roofline": {"bound": w.bound, "achieved": round(kval, 2),
+                                       "peak": round(peak, 1), "frac": round(kval / peak, 4),
+                                       "peak_source": peaks["source"]}}), flush=True)
+
+
 def time_steps(fn, steps: int, warmup: int, ws: int):
     """CUDA-event time of exactly `steps` calls (after `warmup`), max over ranks, in ms."""
     import torch
@@ -296,12 +427,21 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gemv", action="store_true", help="skip the GEMV side measurement")
+    ap.add_argument("--config", default=None,
+                    help="run one BASELINE config alone: c1, c2, c3, c4, c5 (M=16), c51, c54")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     ws, rank, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, ws, rank)
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    if args.config:
+        run_config(args, ws, rank, local)
         if ws > 1:
             import torch.distributed as dist
             dist.destroy_process_group()

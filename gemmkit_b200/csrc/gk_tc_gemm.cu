@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             int r_vlo = 0, r_vhi = 0, r_bias = 0;
             ColParam* cp = cparams + acc * BN;
             if constexpr (OUT == Out::Q8) {
-                if (e.scale_axis != AX_N || e.bias_axis == AX_N) {
+                if (e.scale_axis != AX_N) {
                     float s = e.scale;
                     if (e.scale_axis == AX_M)
                         s = row_ok ? e.scales[b * e.scale_bs + grow] : 1.0f;
@@ -298,11 +298,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         if (e.scale_axis == AX_N) {
                             make_scale_param(cok ? e.scales[b * e.scale_bs + gc] : 1.0f, c.se,
                                              c.nms, c.vlo, c.vhi);
-                        } else {
-                            c.se = r_se;
-                            c.nms = r_nms;
-                            c.vlo = r_vlo;
-                            c.vhi = r_vhi;
+                        } else {  // the scale lives in each thread's registers
+                            c.se = 0.0;
+                            c.nms = 0.0;
+                            c.vlo = 0;
+                            c.vhi = 0;
                         }
                         c.bias = (e.bias_axis == AX_N && cok) ? e.bias[b * e.bias_bs + gc] : 0;
                         c.pad = 0;
@@ -340,7 +340,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
                 if constexpr (OUT == Out::Q8) {
                     int r[CH];
-                    if (e.scale_axis == AX_N || e.bias_axis == AX_N) {
+                    if (e.scale_axis == AX_N) {
+                        // per-column scale (and a per-column or per-row bias)
 #pragma unroll
                         for (int i = 0; i < CH; ++i) {
                             const ColParam& pc = cp[c * CH + i];
@@ -348,6 +349,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                             r[i] = requant_one(static_cast<int32_t>(v[i]), bias, pc.se, pc.nms,
                                                pc.vlo, pc.vhi, e.zp, e.lo, e.hi);
                         }
+                    } else if (e.bias_axis == AX_N) {
+                        // per-row (or per-tensor) scale in registers, per-column bias
+#pragma unroll
+                        for (int i = 0; i < CH; ++i)
+                            r[i] = requant_one(static_cast<int32_t>(v[i]), cp[c * CH + i].bias,
+                                               r_se, r_nms, r_vlo, r_vhi, e.zp, e.lo, e.hi);
                     } else {
 #pragma unroll
                         for (int i = 0; i < CH; ++i)
