@@ -25,7 +25,7 @@ __all__ = [
     "prepack_rhs_i8", "prepack_rhs_i8_unchecked", "gemm_i8_packed_b", "gemm_i8_packed_b_unchecked",
     "gemm_i8_packed_b_requant", "gemm_i8_requant_batched", "gemm_i8_requant_batched_ptr",
     "gemm_half_f32", "gemm_bf16_f32_unchecked", "gemm_f16_f32_unchecked",
-    "gemm_half_f32_batched", "set_tile_n", "device_status", "selftest_wait_timeout",
+    "gemm_half_f32_batched", "gemm_i8_noalloc_unchecked", "set_tile_n", "device_status", "selftest_wait_timeout",
 ]
 
 
@@ -400,6 +400,20 @@ def gemm_half_f32_batched(is_f16, batch, m, k, n, alpha, a, rsa, csa, a_bs, b, r
     _check(_lib.load().gk_gemm_half_f32_batched_unchecked(
         _ws(ws), int(is_f16), batch, m, k, n, alpha, a, rsa, csa, a_bs, b, rsb, csb, b_bs, beta,
         c, rsc, csc, c_bs, par.c(), _stream(stream)))
+
+
+# ---- i8 -> i32 without allocation ---------------------------------------------------------
+
+NOALLOC_SCRATCH_BYTES = 16 << 20
+
+
+def gemm_i8_noalloc_unchecked(m, k, n, alpha, a, rsa, csa, b, rsb, csb, beta, c, rsc, csc,
+                              stream=None) -> None:
+    """gemm_i8_unchecked for callers that must not allocate device memory: operand packs use
+    the library's fixed 16 MiB device scratch (shared by all calls; order calls on one
+    stream). Raises GemmkitError(GK_EINVAL) when the packs need more than that."""
+    _check(_lib.load().gk_gemm_i8_noalloc_unchecked(m, k, n, alpha, a, rsa, csa, b, rsb, csb,
+                                                    beta, c, rsc, csc, _stream(stream)))
 
 
 # ---- misc -----------------------------------------------------------------------------------

@@ -84,6 +84,8 @@ SIGNATURES = {
     "gk_gemm_half_f32_batched_unchecked": (i32, [vp, C.c_int, sz, sz, sz, sz, f32, vp, pd, pd,
                                                  pd, vp, pd, pd, pd, f32, vp, pd, pd, pd,
                                                  Parallelism, vp]),
+    "gk_gemm_i8_noalloc_unchecked": (i32, [sz, sz, sz, i32, vp, pd, pd, vp, pd, pd, i32, vp, pd,
+                                           pd, vp]),
     "gk_set_tile_n": (i32, [C.c_int]),
     "gk_selftest_wait_timeout": (i32, [C.c_uint64, vp]),
 }

@@ -470,6 +470,11 @@ int check_scale_value(float s) {
 
 }  // namespace
 
+namespace gk {
+// Records `text` as this thread's gk_last_error() message (for entries in other files).
+int set_last_error(int code, const char* text) { return set_err(code, "%s", text); }
+}  // namespace gk
+
 // ==========================================================================================
 // C ABI
 // ==========================================================================================

@@ -85,4 +85,7 @@ int launch_requant_fill(void* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,
                         int64_t batch, const EpiParams& e, cudaStream_t s);
 int launch_selftest_timeout(uint64_t timeout_ns, cudaStream_t s);
 
+// Sets this thread's gk_last_error() text (gk_api.cu); returns `code`.
+int set_last_error(int code, const char* text);
+
 }  // namespace gk

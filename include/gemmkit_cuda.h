@@ -249,6 +249,24 @@ int gk_gemm_half_f32_batched_unchecked(gk_workspace *ws, int is_f16, size_t batc
  * calls on this thread; the GEMMKIT_CUDA_BN environment knob sets the process default. */
 int gk_set_tile_n(int bn);
 
+/* ---- i8 -> i32 without allocation ------------------------------------------------------ */
+
+/* No counterpart in gemmkit. The i8 -> i32 product of gk_gemm_i8_unchecked (same arguments
+ * minus the workspace and Parallelism, same result bytes) for callers that must not
+ * allocate device memory: hosts that give the GPU a fixed budget through their own
+ * allocator, or latency-critical loops where cudaMalloc / cudaFree could synchronise the
+ * device. Operands that need packing (not K-contiguous or not 16-byte aligned) are packed
+ * into one file-scope device array of GK_NOALLOC_SCRATCH_BYTES, which every GPU that loads
+ * the library holds until exit; a call whose packs need more returns GK_EINVAL. The first
+ * call on a device looks up that array's device address; make it before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race, so order them on one
+ * stream. Never calls cudaMalloc, cudaFree or an allocating library routine. */
+#define GK_NOALLOC_SCRATCH_BYTES (16u << 20)
+int gk_gemm_i8_noalloc_unchecked(size_t m, size_t k, size_t n, int32_t alpha, const int8_t *a,
+                                 ptrdiff_t rsa, ptrdiff_t csa, const int8_t *b, ptrdiff_t rsb,
+                                 ptrdiff_t csb, int32_t beta, int32_t *c, ptrdiff_t rsc,
+                                 ptrdiff_t csc, gk_stream_t stream);
+
 /* ---- self test of the bounded-wait path ----------------------------------------------- */
 
 /* Launch a kernel that waits on an mbarrier no one arrives on, with a `timeout_ns` bound,
