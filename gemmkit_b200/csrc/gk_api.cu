@@ -26,8 +26,8 @@ struct gk_workspace {
 
 struct gk_packed_rhs {
     int device;
-    int8_t* buf;  // n rows of kp bytes: B^T, K-contiguous, zero padded
-    size_t k, n, kp;
+    uint8_t* buf;  // B^T in the tiled layout (gk_engine.h, Operand::slab), zero padded
+    size_t k, n, k_pad, n_pad;  // k_pad: multiple of 128; n_pad: multiple of 256
 };
 
 namespace {
@@ -283,6 +283,7 @@ struct Job {
 struct KOp {  // an operand in the canonical frame: rows x K, element (r, p) at r*rs + p*ks
     const void* p;
     int64_t rows, rs, ks, bs;
+    int64_t slab;  // > 0: the tiled prepacked layout (already device-ready)
 };
 
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
@@ -364,12 +365,13 @@ int execute(const Job& j) {
     else
         swap = llabs(j.csc) > llabs(j.rsc);
 
-    KOp ua{j.a.p, j.m, j.a.rs, j.a.cs, j.a.bs};
+    KOp ua{j.a.p, j.m, j.a.rs, j.a.cs, j.a.bs, 0};
     KOp ub;
     if (j.packed)
-        ub = KOp{j.packed->buf, j.n, static_cast<int64_t>(j.packed->kp), 1, 0};
+        ub = KOp{j.packed->buf, static_cast<int64_t>(j.packed->n_pad), 128, 1, 0,
+                 static_cast<int64_t>(j.packed->n_pad) * 128};
     else
-        ub = KOp{j.b.p, j.n, j.b.cs, j.b.rs, j.b.bs};
+        ub = KOp{j.b.p, j.n, j.b.cs, j.b.rs, j.b.bs, 0};
     KOp ka = swap ? ub : ua, kb = swap ? ua : ub;
     const int64_t Mk = swap ? j.n : j.m, Nk = swap ? j.m : j.n;
 
@@ -379,6 +381,7 @@ int execute(const Job& j) {
     KOp* ops[2] = {&ka, &kb};
     for (int i = 0; i < 2; ++i) {
         KOp& o = *ops[i];
+        if (o.slab) continue;
         if (o.rows == 1 && o.ks == 1 && !(reinterpret_cast<uintptr_t>(o.p) & 15)) o.rs = ldp;
         if (!tma_ready(o, j.k, j.batch, es)) {
             const int64_t nb = (j.batch > 1 && o.bs != 0) ? j.batch : 1;
@@ -399,7 +402,7 @@ int execute(const Job& j) {
             if (gk::launch_pack_kmajor(cur, ldp, dbs, o.p, o.rs, o.ks, o.bs, o.rows, j.k, nb, es,
                                        j.stream))
                 return set_err(GK_ECUDA, "gemmkit: pack kernel launch failed");
-            o = KOp{cur, o.rows, ldp, 1, nb > 1 ? dbs : 0};
+            o = KOp{cur, o.rows, ldp, 1, nb > 1 ? dbs : 0, 0};
             cur += need[i];
         }
     }
@@ -420,8 +423,8 @@ int execute(const Job& j) {
     pr.Nk = Nk;
     pr.K = j.k;
     pr.batch = j.batch;
-    pr.a = gk::Operand{ka.p, ka.rows, ka.rs, ka.bs};
-    pr.b = gk::Operand{kb.p, kb.rows, kb.rs, kb.bs};
+    pr.a = gk::Operand{ka.p, ka.rows, ka.rs, ka.bs, ka.slab};
+    pr.b = gk::Operand{kb.p, kb.rows, kb.rs, kb.bs, kb.slab};
     pr.e = e;
     pr.bn = tile_n_override();
     pr.stream = j.stream;
@@ -712,9 +715,10 @@ int gk_prepack_rhs_i8_unchecked(const int8_t* b, ptrdiff_t rsb, ptrdiff_t csb, s
                        "gemmkit: prepacked RHS of %zux%zu is too large; the pack buffer size "
                        "overflows usize",
                        k, n);
-    gk_packed_rhs* p = new gk_packed_rhs{dev, nullptr, k, n, 0};
-    p->kp = static_cast<size_t>(round_up(static_cast<int64_t>(k), 16));
-    const size_t bytes = p->kp * n;
+    gk_packed_rhs* p = new gk_packed_rhs{dev, nullptr, k, n, 0, 0};
+    p->k_pad = static_cast<size_t>(round_up(static_cast<int64_t>(k), 128));
+    p->n_pad = static_cast<size_t>(round_up(static_cast<int64_t>(n), 256));
+    const size_t bytes = (k && n) ? p->k_pad * p->n_pad : 0;
     if (bytes) {
         if (!b) {
             delete p;
@@ -727,8 +731,8 @@ int gk_prepack_rhs_i8_unchecked(const int8_t* b, ptrdiff_t rsb, ptrdiff_t csb, s
             return cuda_err(e, "prepack allocation");
         }
         // B^T rows (one per column j of B): element (j, p) = b[p*rsb + j*csb]
-        if (gk::launch_pack_kmajor(p->buf, p->kp, 0, b, csb, rsb, 0, n, k, 1, 1,
-                                   static_cast<cudaStream_t>(stream))) {
+        if (gk::launch_pack_tiled(p->buf, p->n_pad, p->k_pad, b, csb, rsb, n, k,
+                                  static_cast<cudaStream_t>(stream))) {
             cudaFree(p->buf);
             delete p;
             return set_err(GK_ECUDA, "gemmkit: pack kernel launch failed");

@@ -70,6 +70,53 @@ int launch_pack_kmajor(void* dst, int64_t dld, int64_t dbs, const void* src, int
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
+// The tiled prepacked layout (gk_engine.h, Operand::slab): byte (r, p) of the rows x K operand
+// goes to block p / 128, row r, 16-byte chunk ((p % 128) / 16) ^ (r % 8). One 32-row x 32-byte
+// tile per block of 32 x 8 threads, read and written coalesced through shared memory.
+__global__ void pack_tiled_kernel(uint8_t* __restrict__ dst, int64_t rows_pad,
+                                  const int8_t* __restrict__ src, int64_t srs, int64_t scs,
+                                  int64_t rows, int64_t K) {
+    __shared__ int8_t tile[32][33];
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32;
+    const int64_t k0 = static_cast<int64_t>(blockIdx.x) * 32;
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    const bool k_fast = (scs == 1) || (srs != 1 && (scs < 0 ? -scs : scs) <= (srs < 0 ? -srs : srs));
+    for (int i = ty; i < 32; i += 8) {
+        int64_t r, k;
+        if (k_fast) {
+            r = r0 + i;
+            k = k0 + tx;
+        } else {
+            r = r0 + tx;
+            k = k0 + i;
+        }
+        int8_t v = 0;
+        if (r < rows && k < K) v = src[r * srs + k * scs];
+        if (k_fast)
+            tile[i][tx] = v;
+        else
+            tile[tx][i] = v;
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int64_t r = r0 + i, k = k0 + tx;  // always inside [rows_pad, k_pad)
+        const int64_t kb = k >> 7, c = k & 127;
+        const int64_t off = kb * rows_pad * 128 + r * 128 + ((((c >> 4) ^ (r & 7)) << 4) | (c & 15));
+        dst[off] = static_cast<uint8_t>(tile[i][tx]);
+    }
+}
+
+int launch_pack_tiled(uint8_t* dst, int64_t rows_pad, int64_t k_pad, const int8_t* src,
+                      int64_t srs, int64_t scs, int64_t rows, int64_t K, cudaStream_t st) {
+    if (rows_pad == 0 || k_pad == 0) return 0;
+    if ((rows_pad % 32) || (k_pad % 128)) return 1;
+    dim3 block(32, 8);
+    dim3 grid(static_cast<unsigned>(k_pad / 32), static_cast<unsigned>(rows_pad / 32));
+    if (grid.y > 65535u) return 1;
+    pack_tiled_kernel<<<grid, block, 0, st>>>(dst, rows_pad, src, srs, scs, rows, K);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
 __global__ void scale_c_i32_kernel(int32_t* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,
                                    int32_t beta) {
     const int64_t total = m * n;

@@ -39,6 +39,11 @@ struct GemmParams {
     int32_t K, batch;
     int32_t tiles_m, tiles_n, tiles_per_batch, num_tiles, num_kb, group_m;
     int32_t a_batched, b_batched;
+    // Operands held in the tiled prepacked layout (see Operand::slab) are fetched with 1-D
+    // bulk copies from these bases instead of through their tensor maps (nullptr = TMA).
+    const uint8_t* a_tiled;
+    const uint8_t* b_tiled;
+    int64_t a_slab, b_slab;  // bytes between consecutive 128-byte K blocks
     uint64_t timeout_ns;
     unsigned int* status;
     EpiParams e;
@@ -49,6 +54,12 @@ struct GemmParams {
 struct Operand {
     const void* ptr;
     int64_t rows, ld, bs;
+    // slab > 0: the tiled prepacked layout. K is cut into 128-byte blocks; block kb is one
+    // contiguous slab of `slab` bytes holding every (padded) row's 128 bytes at a 128-byte
+    // stride, each row's 16-byte chunks already in the 128-byte-swizzle order
+    // (chunk j of row r stored at j ^ (r % 8)). Any 8-row-aligned run of rows of one block is
+    // then a contiguous copy that lands in shared memory exactly as the MMA reads it.
+    int64_t slab;
 };
 
 struct TcProblem {
@@ -71,6 +82,10 @@ unsigned int* device_status_ptr();
 int sm_count();
 
 // Auxiliary kernels (gk_aux.cu).
+// The tiled prepacked layout (Operand::slab) of a rows x K operand whose element (r, p) is at
+// src[r*srs + p*scs]; rows_pad / k_pad are multiples of 256 / 128 and the padding is zero.
+int launch_pack_tiled(uint8_t* dst, int64_t rows_pad, int64_t k_pad, const int8_t* src,
+                      int64_t srs, int64_t scs, int64_t rows, int64_t K, cudaStream_t s);
 // dst[e][r][k] = src[e*sbs + r*srs + k*scs] for k < K, 0 for K <= k < ld (element size es).
 int launch_pack_kmajor(void* dst, int64_t dld, int64_t dbs, const void* src, int64_t srs,
                        int64_t scs, int64_t sbs, int64_t rows, int64_t K, int64_t batch, int es,

@@ -160,8 +160,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
-        prefetch_tmap(&tmA);
-        prefetch_tmap(&tmB);
+        if (!p.a_tiled) prefetch_tmap(&tmA);
+        if (!p.b_tiled) prefetch_tmap(&tmB);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -189,8 +189,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-                    tma_load_3d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BKE, tm * BM, za);
-                    tma_load_3d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BKE, tn * BN, zb);
+                    if (p.a_tiled)
+                        bulk_load(sA + stage * C::A_BYTES,
+                                  p.a_tiled + kb * p.a_slab + static_cast<int64_t>(tm) * BM * BKB,
+                                  C::A_BYTES, &full[stage]);
+                    else
+                        tma_load_3d(sA + stage * C::A_BYTES, &tmA, &full[stage], kb * BKE,
+                                    tm * BM, za);
+                    if (p.b_tiled)
+                        bulk_load(sB + stage * C::B_BYTES,
+                                  p.b_tiled + kb * p.b_slab + static_cast<int64_t>(tn) * BN * BKB,
+                                  C::B_BYTES, &full[stage]);
+                    else
+                        tma_load_3d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BKE,
+                                    tn * BN, zb);
                     issued |= 1u << stage;
                     last_par = (last_par & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) {
@@ -544,10 +556,21 @@ static int launch_one(const TcProblem& pr, GemmParams gp, char* err, size_t errl
     using C = TileCfg<OUT, BN>;
     constexpr int ES = (KIND == Kind::I8) ? 1 : 2;
     CUtensorMap ta, tb;
-    int rc = encode_operand(&ta, pr.a, pr.K, pr.batch, ES, BM, err, errlen);
-    if (rc) return rc;
-    rc = encode_operand(&tb, pr.b, pr.K, pr.batch, ES, BN, err, errlen);
-    if (rc) return rc;
+    memset(&ta, 0, sizeof(ta));
+    memset(&tb, 0, sizeof(tb));
+    int rc = 0;
+    if (pr.a.slab == 0 && (rc = encode_operand(&ta, pr.a, pr.K, pr.batch, ES, BM, err, errlen)))
+        return rc;
+    if (pr.b.slab == 0 && (rc = encode_operand(&tb, pr.b, pr.K, pr.batch, ES, BN, err, errlen)))
+        return rc;
+    if (pr.b.slab && (pr.b.rows % BN)) {
+        snprintf(err, errlen, "gemmkit: internal error: tiled operand rows not padded to %d", BN);
+        return 1;
+    }
+    gp.a_tiled = pr.a.slab ? static_cast<const uint8_t*>(pr.a.ptr) : nullptr;
+    gp.b_tiled = pr.b.slab ? static_cast<const uint8_t*>(pr.b.ptr) : nullptr;
+    gp.a_slab = pr.a.slab;
+    gp.b_slab = pr.b.slab;
     auto kern = tc_gemm_kernel<KIND, OUT, BN>;
     static int attr_done[64] = {0};
     int dev = 0;
