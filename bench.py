@@ -159,10 +159,26 @@ class C2:
         self.ops = 2.0 * m * n * k
         self.algo_bytes = m * k + n * k + m * n + 8 * n  # A + B + C + bias + scales
 
+        self.calls = [self._call(s) for s in self.sets]
+
+    def _call(self, st):
+        """The C-ABI call with its ctypes arguments built once (the device-resident loop)."""
+        import ctypes as C
+
+        import torch
+
+        from gemmkit_b200 import _lib
+        a, _, packed, req, c = st
+        fn = _lib.load().gk_gemm_i8_packed_b_requant_unchecked
+        args = (None, self.m, a.data_ptr(), self.k, 1, packed.h, C.byref(req.c()), c.data_ptr(),
+                1, self.m, 0, _lib.Parallelism(0, 0),
+                C.c_void_p(torch.cuda.current_stream().cuda_stream))
+        return fn, args
+
     def step(self, i: int, stream=None):
-        a, _, packed, req, c = self.sets[i % ROTATE]
-        self.gk.gemm_i8_packed_b_requant(self.m, a.data_ptr(), self.k, 1, packed, req,
-                                         c.data_ptr(), 1, self.m, stream=stream)
+        fn, args = self.calls[i % ROTATE]
+        if fn(*args) != 0:
+            raise RuntimeError(self.gk._lib.last_error())
 
     launches_per_step = 1
 
@@ -190,11 +206,51 @@ class C5:
             self.sets.append((a, packed, req, c))
         torch.cuda.synchronize()
         self.bytes = self.k * self.n + M * self.k + M * self.n + 4 * self.n
+        import ctypes as C
+
+        from gemmkit_b200 import _lib
+        fn = _lib.load().gk_gemm_i8_packed_b_requant_unchecked
+        self.calls = [(fn, (None, M, a.data_ptr(), self.k, 1, packed.h, C.byref(req.c()),
+                            c.data_ptr(), self.n, 1, 0, _lib.Parallelism(0, 0),
+                            C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+                      for (a, packed, req, c) in self.sets]
 
     def step(self, i: int, stream=None):
-        a, packed, req, c = self.sets[i % ROTATE]
-        self.gk.gemm_i8_packed_b_requant(self.M, a.data_ptr(), self.k, 1, packed, req,
-                                         c.data_ptr(), self.n, 1, stream=stream)
+        fn, args = self.calls[i % ROTATE]
+        if fn(*args) != 0:
+            raise RuntimeError(self.gk._lib.last_error())
+
+    def graph_ms(self, reps: int = 100, ws: int = 1) -> float:
+        """Device time per call of `reps` calls replayed from one CUDA graph (the way a
+        launch-bound decode loop runs), max over ranks."""
+        import torch
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            calls = self.calls
+            self.calls = [(fn, args[:-1] + (__import__("ctypes").c_void_p(s.cuda_stream),))
+                          for fn, args in calls]
+            for i in range(8):
+                self.step(i)
+            s.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for i in range(reps):
+                    self.step(i)
+            self.calls = calls
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        barrier(ws)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(ws)
+        return max_over_ranks(e0.elapsed_time(e1) / (5 * reps), ws)
 
 
 class C1:
@@ -310,6 +366,9 @@ def run_config(args, ws, rank, local):
         w = C2(7 + rank)
         w.unit, w.bound, w.work, w.bytes = "TOPS", "tensor", w.ops, w.algo_bytes
     ms = time_steps(w.step, args.steps, args.warmup, ws) / args.steps
+    eager_ms = ms
+    if isinstance(w, C5):
+        ms = w.graph_ms(100, ws)
     if w.unit == "GB/s":
         val = ws * w.bytes / (ms * 1e-3) / 1e9
         peak, kval = peaks["hbm_gbs"], w.bytes / (ms * 1e-3) / 1e9
@@ -319,7 +378,8 @@ def run_config(args, ws, rank, local):
         peak = peaks["bf16_tflops"] * (2.0 if w.unit == "TOPS" else 1.0)
     if rank == 0:
         print(json.dumps({"config": cfg, "workload": w.name, "value": round(val, 2),
-                          "unit": w.unit, "ms_per_step": round(ms, 5), "n_gpus": ws,
+                          "unit": w.unit, "ms_per_step": round(ms, 5),
+                          "ms_per_step_eager": round(eager_ms, 5), "n_gpus": ws,
                           "steps": args.steps, "warmup": args.warmup,
                           "tops_or_tflops": round(ws * w.work / (ms * 1e-3) / 1e12, 2),
                           "gbs": round(ws * w.bytes / (ms * 1e-3) / 1e9, 1),
@@ -487,10 +547,13 @@ def main():
         gemv = {}
         for M in (1, 4, 16):
             g = C5(M, seed=99 + rank)
-            gms = time_steps(g.step, 500, 10, ws) / 500
+            gms = g.graph_ms(100, ws)
+            pms = time_steps(g.step, 300, 10, ws) / 300
             gemv[f"M{M}"] = {"gbs": round(ws * g.bytes / (gms * 1e-3) / 1e9, 1),
                              "us_per_call": round(gms * 1e3, 2),
-                             "frac_hbm": round(g.bytes / (gms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)}
+                             "frac_hbm": round(g.bytes / (gms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                             "timing": "CUDA-graph replay of 100 calls",
+                             "us_per_call_eager": round(pms * 1e3, 2)}
             del g
         torch.cuda.empty_cache()
 

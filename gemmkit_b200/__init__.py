@@ -138,9 +138,12 @@ class Workspace:
         self.h = h
 
     def __del__(self):
-        if getattr(self, "h", None) is not None and self.h.value:
-            _lib.load().gk_workspace_free(self.h)
-            self.h = None
+        try:
+            if getattr(self, "h", None) is not None and self.h.value:
+                _lib.load().gk_workspace_free(self.h)
+                self.h = None
+        except Exception:  # interpreter shutdown
+            pass
 
 
 def _ws(ws: Optional[Workspace]):
@@ -179,6 +182,16 @@ class Requantize:
     relu: bool = False
 
     def c(self) -> RequantC:
+        key = (self.scale.value, self.scale.axis, id(self.scale.vector), self.zero_point,
+               id(self.bias), self.bias_axis, self.relu)
+        cached = self.__dict__.get("_c_cache")
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        r = self._build_c()
+        self.__dict__["_c_cache"] = (key, r)
+        return r
+
+    def _build_c(self) -> RequantC:
         r = RequantC()
         r.scale = self.scale.value
         r.scale_axis = self.scale.axis
@@ -281,9 +294,12 @@ class PackedRhs:
         return _lib.load().gk_packed_rhs_cols(self.h)
 
     def __del__(self):
-        if getattr(self, "h", None) is not None and self.h.value:
-            _lib.load().gk_packed_rhs_free(self.h)
-            self.h = None
+        try:
+            if getattr(self, "h", None) is not None and self.h.value:
+                _lib.load().gk_packed_rhs_free(self.h)
+                self.h = None
+        except Exception:  # interpreter shutdown: the library may already be unloaded
+            pass
 
 
 def prepack_rhs_i8(b: MatRef, stream=None, sync: bool = True) -> PackedRhs:

@@ -20,8 +20,11 @@ using gk::AX_NONE;
 
 struct gk_workspace {
     int device;
-    void* ptr;
+    void* ptr;  // operand packs + stream-K partial accumulators
     size_t cap;
+    uint32_t* ctr;  // stream-K arrival counters: zeroed when allocated, epoch-tagged after
+    size_t ctr_cap;
+    uint32_t epoch;
 };
 
 struct gk_packed_rhs {
@@ -69,6 +72,17 @@ int check_device(int* dev_out) {
         return set_err(GK_ENODEV, "gemmkit: the CUDA engine needs an sm_100 (B200) device");
     if (dev_out) *dev_out = dev;
     return GK_OK;
+}
+
+// GEMMKIT_CUDA_STREAMK=1 enables the stream-K tail (off by default: its partial reductions
+// cost more than the last wave they rebalance on the shapes measured so far).
+bool streamk_enabled() {
+    static int env = -1;
+    if (env == -1) {
+        const char* s = getenv("GEMMKIT_CUDA_STREAMK");
+        env = (s && s[0] == '1') ? 1 : 0;
+    }
+    return env == 1;
 }
 
 int tile_n_override() {
@@ -221,7 +235,7 @@ std::string rust_f32(float x) {
 gk_workspace* default_ws(int dev) {
     thread_local gk_workspace* tls[64] = {nullptr};
     if (!tls[dev & 63]) {
-        tls[dev & 63] = new gk_workspace{dev, nullptr, 0};
+        tls[dev & 63] = new gk_workspace{dev, nullptr, 0, nullptr, 0, 0};
     }
     return tls[dev & 63];
 }
@@ -248,6 +262,38 @@ int ws_ensure(gk_workspace* ws, size_t bytes, void** out) {
         ws->cap = cap;
     }
     *out = ws->ptr;
+    return GK_OK;
+}
+
+// Stream-K counters: `words` zero-initialised 32-bit words, and the epoch of the next launch
+// (1 .. 2^24 - 1; on wrap-around the counters are cleared again on `st`).
+int ctr_ensure(gk_workspace* ws, size_t words, cudaStream_t st, uint32_t* epoch) {
+    const size_t bytes = words * sizeof(uint32_t);
+    if (ws->ctr_cap < bytes) {
+        if (ws->ctr) {
+            cudaDeviceSynchronize();
+            cudaFree(ws->ctr);
+            ws->ctr = nullptr;
+            ws->ctr_cap = 0;
+        }
+        size_t cap = (bytes + 4095) & ~static_cast<size_t>(4095);
+        cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&ws->ctr), cap);
+        if (e == cudaSuccess) e = cudaMemset(ws->ctr, 0, cap);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            if (ws->ctr) cudaFree(ws->ctr);
+            ws->ctr = nullptr;
+            return cuda_err(e, "workspace counter allocation");
+        }
+        ws->ctr_cap = cap;
+        ws->epoch = 0;
+    }
+    ws->epoch = ws->epoch >= 0xFFFFFFu ? 1u : ws->epoch + 1u;
+    if (ws->epoch == 1u && ws->ctr_cap) {
+        cudaError_t e = cudaMemsetAsync(ws->ctr, 0, ws->ctr_cap, st);
+        if (e != cudaSuccess) return cuda_err(e, "workspace counter reset");
+    }
+    *epoch = ws->epoch;
     return GK_OK;
 }
 
@@ -326,6 +372,7 @@ int execute(const Job& j) {
     e.zp = j.zp;
     e.lo = j.lo;
     e.hi = j.hi;
+    e.relu = j.out == gk::Out::Q8 && j.lo > (j.hi == 255 ? 0 : -128);
 
     // Degenerate products: gemmkit's scale_c_int (k == 0 or alpha == 0) and
     // requant_degenerate (k == 0).
@@ -388,24 +435,6 @@ int execute(const Job& j) {
             need[i] = round_up(o.rows * ldp * es * nb, 256);
         }
     }
-    if (need[0] || need[1]) {
-        gk_workspace* ws = j.ws ? j.ws : default_ws(dev);
-        void* base = nullptr;
-        rc = ws_ensure(ws, static_cast<size_t>(need[0] + need[1]), &base);
-        if (rc) return rc;
-        char* cur = static_cast<char*>(base);
-        for (int i = 0; i < 2; ++i) {
-            if (!need[i]) continue;
-            KOp& o = *ops[i];
-            const int64_t nb = (j.batch > 1 && o.bs != 0) ? j.batch : 1;
-            const int64_t dbs = o.rows * ldp;
-            if (gk::launch_pack_kmajor(cur, ldp, dbs, o.p, o.rs, o.ks, o.bs, o.rows, j.k, nb, es,
-                                       j.stream))
-                return set_err(GK_ECUDA, "gemmkit: pack kernel launch failed");
-            o = KOp{cur, o.rows, ldp, 1, nb > 1 ? dbs : 0, 0};
-            cur += need[i];
-        }
-    }
 
     e.out = j.c;
     e.ldo = swap ? j.csc : j.rsc;
@@ -417,19 +446,50 @@ int execute(const Job& j) {
             ((e.ldo * eso) % 16 == 0 || Mk == 1) && (j.batch <= 1 || (j.cbs * eso) % 16 == 0);
 
     gk::TcProblem pr;
+    memset(&pr, 0, sizeof(pr));
     pr.kind = j.kind;
-    pr.out = j.out;
+    pr.out = (j.out == gk::Out::Q8 && j.hi == 255) ? gk::Out::U8 : j.out;
     pr.Mk = Mk;
     pr.Nk = Nk;
     pr.K = j.k;
     pr.batch = j.batch;
-    pr.a = gk::Operand{ka.p, ka.rows, ka.rs, ka.bs, ka.slab};
-    pr.b = gk::Operand{kb.p, kb.rows, kb.rs, kb.bs, kb.slab};
     pr.e = e;
     pr.bn = tile_n_override();
     pr.stream = j.stream;
+    gk::TcPlan plan;
+    gk::plan_tc_gemm(pr, streamk_enabled(), &plan);
+    const int64_t part_bytes = round_up(plan.part_words * 4, 256);
+
+    gk_workspace* ws = j.ws ? j.ws : default_ws(dev);
+    char* base = nullptr;
+    if (need[0] + need[1] + part_bytes) {
+        void* vb = nullptr;
+        rc = ws_ensure(ws, static_cast<size_t>(need[0] + need[1] + part_bytes), &vb);
+        if (rc) return rc;
+        base = static_cast<char*>(vb);
+    }
+    if (plan.sk_iters > 0) {
+        rc = ctr_ensure(ws, static_cast<size_t>(plan.ctr_words), j.stream, &pr.sk_epoch);
+        if (rc) return rc;
+        pr.sk_ctr = ws->ctr;
+        pr.sk_part = reinterpret_cast<uint32_t*>(base + need[0] + need[1]);
+    }
+    char* cur = base;
+    for (int i = 0; i < 2; ++i) {
+        if (!need[i]) continue;
+        KOp& o = *ops[i];
+        const int64_t nb = (j.batch > 1 && o.bs != 0) ? j.batch : 1;
+        const int64_t dbs = o.rows * ldp;
+        if (gk::launch_pack_kmajor(cur, ldp, dbs, o.p, o.rs, o.ks, o.bs, o.rows, j.k, nb, es,
+                                   j.stream))
+            return set_err(GK_ECUDA, "gemmkit: pack kernel launch failed");
+        o = KOp{cur, o.rows, ldp, 1, nb > 1 ? dbs : 0, 0};
+        cur += need[i];
+    }
+    pr.a = gk::Operand{ka.p, ka.rows, ka.rs, ka.bs, ka.slab};
+    pr.b = gk::Operand{kb.p, kb.rows, kb.rs, kb.bs, kb.slab};
     char err[512] = "";
-    rc = gk::launch_tc_gemm(pr, err, sizeof(err));
+    rc = gk::launch_tc_gemm_planned(pr, plan, err, sizeof(err));
     if (rc) return set_err(rc, "%s", err);
     return GK_OK;
 }
@@ -507,16 +567,15 @@ int gk_workspace_create(gk_workspace** out) {
     if (!out) return set_err(GK_EINVAL, "gemmkit: null output pointer");
     int dev = 0;
     cudaGetDevice(&dev);
-    *out = new gk_workspace{dev, nullptr, 0};
+    *out = new gk_workspace{dev, nullptr, 0, nullptr, 0, 0};
     return GK_OK;
 }
 
 void gk_workspace_free(gk_workspace* ws) {
     if (!ws) return;
-    if (ws->ptr) {
-        cudaDeviceSynchronize();
-        cudaFree(ws->ptr);
-    }
+    if (ws->ptr || ws->ctr) cudaDeviceSynchronize();
+    if (ws->ptr) cudaFree(ws->ptr);
+    if (ws->ctr) cudaFree(ws->ctr);
     delete ws;
 }
 

@@ -15,7 +15,7 @@
 namespace gk {
 
 enum class Kind : int { I8 = 0, F16 = 1, BF16 = 2 };
-enum class Out : int { I32 = 0, Q8 = 1, F32 = 2 };
+enum class Out : int { I32 = 0, Q8 = 1, F32 = 2, U8 = 3 };  // Q8: i8 requant, U8: u8 requant
 enum Axis : int { AX_NONE = 0, AX_M = 1, AX_N = 2 };
 
 struct EpiParams {
@@ -31,6 +31,7 @@ struct EpiParams {
     int64_t scale_bs;
     float scale;
     int32_t zp, lo, hi;  // lo already raised to clamp(zp) under ReLU
+    int32_t relu;        // apply the raised lower clamp (the band's own clamp is a saturation)
     int32_t vec;         // cso == 1 and every row start 16-byte aligned
 };
 
@@ -44,6 +45,17 @@ struct GemmParams {
     const uint8_t* a_tiled;
     const uint8_t* b_tiled;
     int64_t a_slab, b_slab;  // bytes between consecutive 128-byte K blocks
+    // Stream-K tail: tiles [0, dp_tiles) run whole, round-robin over the CTAs; the K blocks
+    // of the remaining tiles are spread evenly over all CTAs. A tile cut between CTAs leaves
+    // 32-bit partial accumulators in sk_part; the last CTA to finish a 32-row x WCOLS region
+    // (counted in sk_ctr, tagged with sk_epoch so stale counts are ignored) sums them in slot
+    // order and runs the epilogue.
+    int32_t dp_tiles;
+    int32_t sk_maxc;   // partial slots per stream-K tile
+    int64_t sk_iters;  // (num_tiles - dp_tiles) * num_kb, 0 = no stream-K
+    uint32_t* sk_part;
+    uint32_t* sk_ctr;
+    uint32_t sk_epoch;
     uint64_t timeout_ns;
     unsigned int* status;
     EpiParams e;
@@ -70,7 +82,23 @@ struct TcProblem {
     EpiParams e;
     int bn;  // 0 = heuristic
     cudaStream_t stream;
+    // Scratch for a stream-K tail (see GemmParams); nullptr = no stream-K.
+    uint32_t* sk_part;
+    uint32_t* sk_ctr;
+    uint32_t sk_epoch;
 };
+
+// Launch geometry chosen for a problem (tile width, grid, stream-K split and the scratch it
+// needs). plan_tc_gemm fills it; allow_sk = false plans without a stream-K tail.
+struct TcPlan {
+    int bn, nepi, tiles_m, tiles_n, num_tiles, num_kb, grid;
+    int dp_tiles, sk_maxc;
+    int64_t sk_iters;
+    int64_t part_words;  // 32-bit words of sk_part
+    int64_t ctr_words;   // 32-bit words of sk_ctr
+};
+void plan_tc_gemm(const TcProblem& p, bool allow_sk, TcPlan* plan);
+int launch_tc_gemm_planned(const TcProblem& p, const TcPlan& plan, char* err, size_t errlen);
 
 // Launch the tcgen05 GEMM for `p` (all operands already TMA-compatible). Returns a GK_*
 // status and fills `err` on failure.

@@ -31,67 +31,88 @@
 
 namespace gk {
 
-constexpr int BM = 128;        // MMA M (TMEM lanes)
-constexpr int BKB = 128;       // bytes of K per stage and row (one 128-byte swizzle atom)
-constexpr int MMA_KB = 32;     // bytes of K per tcgen05.mma (kind::i8 K=32, kind::f16 K=16)
-constexpr int NTHREADS = 192;  // 6 warps
+constexpr int BM = 128;     // MMA M (TMEM lanes)
+constexpr int BKB = 128;    // bytes of K per stage and row (one 128-byte swizzle atom)
+constexpr int MMA_KB = 32;  // bytes of K per tcgen05.mma (kind::i8 K=32, kind::f16 K=16)
 constexpr int SMEM_LIMIT = 232448;
 
 template <Out OUT, int BN>
 struct TileCfg {
+    static constexpr int NEPI = BN >= 64 ? 8 : 4;      // epilogue warps
+    static constexpr int THREADS = 64 + 32 * NEPI;     // + producer warp + MMA warp
+    static constexpr int WCOLS = BN / (NEPI / 4);      // accumulator columns per epilogue warp
+    static constexpr int CH = WCOLS < 32 ? WCOLS : 32;  // TMEM columns per tcgen05.ld
+    static constexpr int NCH = WCOLS / CH;
     static constexpr int A_BYTES = BM * BKB;
     static constexpr int B_BYTES = BN * BKB;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int CP_BYTES = (OUT == Out::Q8) ? 2 * BN * 32 : 0;  // column params x2
+    static constexpr bool QUANT = (OUT == Out::Q8 || OUT == Out::U8);
+    static constexpr int CP_BYTES = QUANT ? 2 * BN * 32 : 0;  // column params, x2 buffers
     static constexpr int BAR_BYTES = 256;
     static constexpr int RAW_STAGES = (SMEM_LIMIT - 1024 - BAR_BYTES - CP_BYTES) / STAGE_BYTES;
-    static constexpr int STAGES = RAW_STAGES > 10 ? 10 : RAW_STAGES;
+    static constexpr int STAGES = RAW_STAGES > 12 ? 12 : RAW_STAGES;
     static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + CP_BYTES;
     static constexpr int TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
-    static constexpr int CH = BN < 32 ? BN : 32;  // TMEM columns per tcgen05.ld
     static_assert(STAGES >= 2, "shared memory too small");
     static_assert(SMEM <= SMEM_LIMIT, "shared memory budget");
+    static_assert(2 * STAGES + 7 <= BAR_BYTES / 8 - 1, "barrier area");
 };
 
-// Per-scale constants of the exact requant (see requant_one).
+// Per-scale constants of the exact requant (see requant_q).
 struct alignas(16) ColParam {
-    double se;    // min(scale, 2048), exact
-    double nms;   // -(2^52 + 2^31) * se, exact (22-bit x 24-bit significands)
-    int32_t vlo;  // accumulator clamp [vlo, vhi] that keeps every result while bounding |p|
-    int32_t vhi;
-    int32_t bias;
-    int32_t pad;
+    double se;           // min(scale, 2048), exact
+    double nms;          // -(2^52 + 2^31) * se, exact (22-bit x 24-bit significands)
+    uint32_t ulo, uhi;   // accumulator clamp [vlo, vhi], offset by 2^31 (unsigned domain)
+    uint32_t bias_plus;  // bias + 2^31 (mod 2^32)
+    uint32_t pad;
 };
 
-__device__ __forceinline__ void make_scale_param(float s, double& se, double& nms, int& vlo,
-                                                 int& vhi) {
+__device__ __forceinline__ void make_scale_param(float s, double& se, double& nms, uint32_t& ulo,
+                                                 uint32_t& uhi) {
     const double s64 = static_cast<double>(s);
     se = s64 < 2048.0 ? s64 : 2048.0;
     nms = -(4503601774854144.0 * se);
     const double vs = ceil(2048.0 / se) + 1.0;
-    vhi = vs >= 2147483647.0 ? 2147483647 : static_cast<int>(vs);
-    vlo = vhi == 2147483647 ? (-2147483647 - 1) : -vhi - 1;
+    const int vhi = vs >= 2147483647.0 ? 2147483647 : static_cast<int>(vs);
+    const int vlo = vhi == 2147483647 ? (-2147483647 - 1) : -vhi - 1;
+    ulo = static_cast<uint32_t>(vlo) + 0x80000000u;
+    uhi = static_cast<uint32_t>(vhi) + 0x80000000u;
 }
 
-// clamp(zp + rne(fl64(f64(v) * f64(scale))), lo, hi) for v = acc +wrap bias, exactly:
-//  1. v is clamped to [vlo, vhi]. The map is monotone in v (scale > 0), and |v| beyond
-//     vhi ~ 2048/scale already drives |v*scale| >= 2048, past any clamp band, so the clamp
-//     changes no result; it bounds |v*se| <= 2048 + 3*se <= 8192. For scale > 2048 the
+// zp + rne(fl64(f64(v) * f64(scale))) for v = acc +wrap bias, exactly (the caller clamps to
+// the output band). gemmkit's KRequantize::apply (gemmkit/src/kernel/epilogue.rs:810-830):
+//  1. u = acc + bias + 2^31 (mod 2^32) is v + 2^31 as an unsigned number, so the unsigned clamp
+//     to [vlo, vhi] + 2^31 is the signed clamp of v. The map is monotone in v (scale > 0), and
+//     |v| beyond vhi ~ 2048/scale already drives |v*scale| >= 2048, past any clamp band, so the
+//     clamp changes no result; it bounds |v*se| <= 2048 + 3*se <= 8192. For scale > 2048 the
 //     band is v in [-3, 2] with se = 2048 and every v != 0 still saturates, as with scale.
-//  2. d = 2^52 + 2^31 + v is exact (built from bits); fma(d, se, -(2^52 + 2^31)*se) has the
-//     exact value v*se and rounds once: it is the reference's f64 product fl64(v*scale).
-//  3. p + 1.5*2^52 rounds p to the nearest integer, ties to even (the reference's 2^52
-//     trick, gemmkit/src/kernel/epilogue.rs:886-897); |p| <= 8192 leaves the integer in the
-//     low word. zp joins after rounding, in integer, then the clamp.
-__device__ __forceinline__ int requant_one(int32_t acc, int32_t bias, double se, double nms,
-                                           int vlo, int vhi, int zp, int lo, int hi) {
-    int v = static_cast<int>(static_cast<uint32_t>(acc) + static_cast<uint32_t>(bias));
-    v = min(max(v, vlo), vhi);
-    const double d = __hiloint2double(0x43300000, v ^ static_cast<int>(0x80000000u));
+//  2. d = 2^52 + u = 2^52 + 2^31 + v is exact (built from bits); fma(d, se, -(2^52+2^31)*se)
+//     has the exact value v*se and rounds once: the reference's f64 product fl64(v*scale).
+//  3. p + 1.5*2^52 rounds p to the nearest integer, ties to even (the reference's 2^52 trick,
+//     gemmkit/src/kernel/epilogue.rs:886-897); |p| <= 8192 leaves the integer in the low word.
+//     zp joins after rounding, in integer.
+__device__ __forceinline__ int requant_q(uint32_t acc, uint32_t bias_plus, double se, double nms,
+                                         uint32_t ulo, uint32_t uhi, int zp) {
+    uint32_t u = acc + bias_plus;
+    u = min(max(u, ulo), uhi);
+    const double d = __hiloint2double(0x43300000, static_cast<int>(u));
     const double p = __fma_rn(d, se, nms);
     const double y = __dadd_rn(p, 6755399441055744.0);
-    const int q = __double2loint(y) + zp;
-    return min(max(q, lo), hi);
+    return __double2loint(y) + zp;
+}
+
+// Four values saturated to the output band and packed little-endian (x0 in the low byte).
+template <bool U8>
+__device__ __forceinline__ uint32_t pack4_sat(int x0, int x1, int x2, int x3) {
+    uint32_t t, d;
+    if constexpr (U8) {
+        asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(t) : "r"(x3), "r"(x2), "r"(0));
+        asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(x1), "r"(x0), "r"(t));
+    } else {
+        asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(t) : "r"(x3), "r"(x2), "r"(0));
+        asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(x1), "r"(x0), "r"(t));
+    }
+    return d;
 }
 
 __device__ __forceinline__ void decode_tile(int t, const GemmParams& p, int& b, int& tm,
@@ -107,6 +128,56 @@ __device__ __forceinline__ void decode_tile(int t, const GemmParams& p, int& b, 
     tn = rr / gsize;
 }
 
+// One unit of a CTA's work: K blocks [k0, k1) of `tile`. nctr > 1 marks a stream-K tile cut
+// between nctr CTAs; this CTA holds partial slot `slot` of it.
+struct Work {
+    int tile, k0, k1, slot, nctr;
+};
+
+// The CTA's sequence of work items, computed identically by every role: first the whole tiles
+// blockIdx.x, blockIdx.x + grid, ... below dp_tiles, then this CTA's contiguous share
+// [start(c), start(c + 1)) of the stream-K iterations (sk_iters >= grid, so every share is
+// non-empty and a tile's contributors are consecutive CTAs).
+struct Sched {
+    int cta, G, dp_next;
+    int64_t it, it_end;
+
+    __device__ __forceinline__ explicit Sched(const GemmParams& p) {
+        cta = blockIdx.x;
+        G = gridDim.x;
+        dp_next = cta;
+        it = p.sk_iters > 0 ? start(p, cta) : 0;
+        it_end = p.sk_iters > 0 ? start(p, cta + 1) : 0;
+    }
+    __device__ __forceinline__ int64_t start(const GemmParams& p, int c) const {
+        return (static_cast<int64_t>(c) * p.sk_iters) / G;
+    }
+    // the CTA whose share holds iteration T: the largest c with start(c) <= T
+    __device__ __forceinline__ int owner(const GemmParams& p, int64_t T) const {
+        const int64_t c = ((T + 1) * G + p.sk_iters - 1) / p.sk_iters - 1;
+        return static_cast<int>(c < 0 ? 0 : (c >= G ? G - 1 : c));
+    }
+    __device__ __forceinline__ bool next(const GemmParams& p, Work& w) {
+        if (dp_next < p.dp_tiles) {
+            w = Work{dp_next, 0, p.num_kb, 0, 1};
+            dp_next += G;
+            return true;
+        }
+        if (it < it_end) {
+            const int skt = static_cast<int>(it / p.num_kb);
+            const int k0 = static_cast<int>(it - static_cast<int64_t>(skt) * p.num_kb);
+            const int64_t left = it_end - it;
+            const int k1 = left < p.num_kb - k0 ? k0 + static_cast<int>(left) : p.num_kb;
+            const int64_t T0 = static_cast<int64_t>(skt) * p.num_kb;
+            const int cf = owner(p, T0), cl = owner(p, T0 + p.num_kb - 1);
+            w = Work{p.dp_tiles + skt, k0, k1, cta - cf, cl - cf + 1};
+            it += k1 - k0;
+            return true;
+        }
+        return false;
+    }
+};
+
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           unsigned int* status, unsigned int where,
                                           uint64_t timeout) {
@@ -114,14 +185,129 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     return !__any_sync(0xffffffffu, !ok);
 }
 
+// The epilogue of one chunk of CH accumulator columns held by this thread (its row `grow`),
+// starting at column gc of the output.
+template <Out OUT, int CH>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], const GemmParams& p,
+                                               const EpiParams& e, int64_t obase, int64_t gc,
+                                               const ColParam* cp, double r_se, double r_nms,
+                                               uint32_t r_ulo, uint32_t r_uhi, uint32_t r_bp) {
+    const bool full_chunk = gc + CH <= p.Nk;
+    if constexpr (OUT == Out::Q8 || OUT == Out::U8) {
+        constexpr bool U8 = OUT == Out::U8;
+        int q[CH];
+        if (e.scale_axis == AX_N) {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) {
+                const ColParam& pc = cp[i];
+                const uint32_t bp = e.bias_axis == AX_N ? pc.bias_plus : r_bp;
+                q[i] = requant_q(v[i], bp, pc.se, pc.nms, pc.ulo, pc.uhi, e.zp);
+            }
+        } else if (e.bias_axis == AX_N) {
+#pragma unroll
+            for (int i = 0; i < CH; ++i)
+                q[i] = requant_q(v[i], cp[i].bias_plus, r_se, r_nms, r_ulo, r_uhi, e.zp);
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i)
+                q[i] = requant_q(v[i], r_bp, r_se, r_nms, r_ulo, r_uhi, e.zp);
+        }
+        if (e.relu) {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) q[i] = max(q[i], e.lo);
+        }
+        uint32_t w[CH / 4];
+#pragma unroll
+        for (int g = 0; g < CH / 4; ++g)
+            w[g] = pack4_sat<U8>(q[4 * g], q[4 * g + 1], q[4 * g + 2], q[4 * g + 3]);
+        uint8_t* out = static_cast<uint8_t*>(e.out);
+        if (e.vec && full_chunk) {
+            uint8_t* dst = out + obase + gc;
+#pragma unroll
+            for (int g = 0; g < CH / 16; ++g)
+                st_global_v4(dst + g * 16, w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i)
+                if (gc + i < p.Nk)
+                    out[obase + (gc + i) * e.cso] = static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3)));
+        }
+    } else if constexpr (OUT == Out::I32) {
+        int32_t* out = static_cast<int32_t*>(e.out);
+        uint32_t r[CH];
+        const uint32_t al = static_cast<uint32_t>(e.alpha_i);
+        const uint32_t be = static_cast<uint32_t>(e.beta_i);
+        if (e.vec && full_chunk) {
+            int32_t* dst = out + obase + gc;
+            if (be != 0u) {
+#pragma unroll
+                for (int g = 0; g < CH / 4; ++g) {
+                    const uint4 cv = ld_global_v4(dst + g * 4);
+                    r[g * 4 + 0] = be * cv.x + al * v[g * 4 + 0];
+                    r[g * 4 + 1] = be * cv.y + al * v[g * 4 + 1];
+                    r[g * 4 + 2] = be * cv.z + al * v[g * 4 + 2];
+                    r[g * 4 + 3] = be * cv.w + al * v[g * 4 + 3];
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < CH; ++i) r[i] = al * v[i];
+            }
+#pragma unroll
+            for (int g = 0; g < CH / 4; ++g)
+                st_global_v4(dst + g * 4, r[g * 4], r[g * 4 + 1], r[g * 4 + 2], r[g * 4 + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) {
+                if (gc + i >= p.Nk) continue;
+                int32_t* cptr = out + obase + (gc + i) * e.cso;
+                uint32_t o = al * v[i];
+                if (be != 0u) o += be * static_cast<uint32_t>(*cptr);
+                *cptr = static_cast<int32_t>(o);
+            }
+        }
+    } else {  // F32
+        float* out = static_cast<float*>(e.out);
+        const float al = e.alpha_f, be = e.beta_f;
+        if (e.vec && full_chunk) {
+            float* dst = out + obase + gc;
+#pragma unroll
+            for (int g = 0; g < CH / 4; ++g) {
+                float x0 = al * __uint_as_float(v[g * 4 + 0]);
+                float x1 = al * __uint_as_float(v[g * 4 + 1]);
+                float x2 = al * __uint_as_float(v[g * 4 + 2]);
+                float x3 = al * __uint_as_float(v[g * 4 + 3]);
+                if (be != 0.0f) {
+                    const uint4 cv = ld_global_v4(dst + g * 4);
+                    x0 = __fmaf_rn(be, __uint_as_float(cv.x), x0);
+                    x1 = __fmaf_rn(be, __uint_as_float(cv.y), x1);
+                    x2 = __fmaf_rn(be, __uint_as_float(cv.z), x2);
+                    x3 = __fmaf_rn(be, __uint_as_float(cv.w), x3);
+                }
+                st_global_v4(dst + g * 4, __float_as_uint(x0), __float_as_uint(x1),
+                             __float_as_uint(x2), __float_as_uint(x3));
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) {
+                if (gc + i >= p.Nk) continue;
+                float* cptr = out + obase + (gc + i) * e.cso;
+                float x = al * __uint_as_float(v[i]);
+                if (be != 0.0f) x = __fmaf_rn(be, *cptr, x);
+                *cptr = x;
+            }
+        }
+    }
+}
+
 template <Kind KIND, Out OUT, int BN>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
     using C = TileCfg<OUT, BN>;
     constexpr int STAGES = C::STAGES;
     constexpr int CH = C::CH;
-    constexpr int NCHUNK = BN / CH;
+    constexpr int NCH = C::NCH;
+    constexpr int NEPI_T = 32 * C::NEPI;  // epilogue threads
     constexpr int ES = (KIND == Kind::I8) ? 1 : 2;
     constexpr int BKE = BKB / ES;  // K elements per stage
 
@@ -152,8 +338,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
-            mbar_init(&pready[a], 128);
+            mbar_init(&tempty[a], NEPI_T);
+            mbar_init(&pready[a], NEPI_T);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -178,11 +364,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             int stage = 0;
             uint32_t phase = 0, issued = 0, last_par = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+            Sched sch(p);
+            Work w;
+            while (ok && sch.next(p, w)) {
                 int b, tm, tn;
-                decode_tile(t, p, b, tm, tn);
+                decode_tile(w.tile, p, b, tm, tn);
                 const int za = p.a_batched ? b : 0, zb = p.b_batched ? b : 0;
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = w.k0; kb < w.k1; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status,
                                    GK_DEV_TIMEOUT_PRODUCER, tmo)) {
                         ok = false;
@@ -230,7 +418,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint32_t phase = 0;
             bool ok = true;
             int local = 0;
-            for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
+            Sched sch(p);
+            Work w;
+            for (; ok && sch.next(p, w); ++local) {
                 const int acc = local & 1;
                 const uint32_t aph = (local >> 1) & 1;
                 if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, p.status, GK_DEV_TIMEOUT_MMA,
@@ -240,7 +430,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = w.k0; kb < w.k1; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag, p.status, GK_DEV_TIMEOUT_MMA,
                                    tmo)) {
                         ok = false;
@@ -253,7 +443,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     for (int ks = 0; ks < BKB / MMA_KB; ++ks) {
                         const uint64_t ad = sdesc_kmajor_sw128(a0 + ks * MMA_KB);
                         const uint64_t bd = sdesc_kmajor_sw128(b0 + ks * MMA_KB);
-                        const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
+                        const uint32_t accum = (kb != w.k0 || ks != 0) ? 1u : 0u;
                         if constexpr (KIND == Kind::I8)
                             mma_i8(d, ad, bd, idesc, accum);
                         else
@@ -274,194 +464,184 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_wait(drain, 0, &dummy, p.status, GK_DEV_TIMEOUT_DRAIN, tmo);
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
-        const int q = warp & 3;           // TMEM lane quarter this warp may access
-        const int et = threadIdx.x - 64;  // 0..127
+        // ---------------- epilogue (warps 2 .. 2 + NEPI) ----------------
+        const int q = warp & 3;                             // TMEM lane quarter it may read
+        const int col_base = ((warp - 2) >> 2) * C::WCOLS;  // its share of the tile's columns
+        const int et = threadIdx.x - 64;                    // < NEPI_T, and BN <= NEPI_T
         const EpiParams& e = p.e;
-        int local = 0;
-        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+        const int row = q * 32 + lane;
+        const bool col_params = C::QUANT && (e.scale_axis == AX_N || e.bias_axis == AX_N);
+
+        // Requant parameters of a tile: this thread's row scale / bias (registers) and the
+        // tile's per-column values (column `et`, shared through shared memory). The global
+        // loads of tile t + 1 are issued before tile t is processed, so their latency hides
+        // behind its epilogue; they are turned into ColParams after it.
+        struct Raw {
+            float rscale, cscale;
+            int32_t rbias, cbias;
+        };
+        auto load_raw = [&](int t, Raw& r) {
             int b, tm, tn;
             decode_tile(t, p, b, tm, tn);
+            const int64_t grow = static_cast<int64_t>(tm) * BM + row;
+            const int64_t gc = static_cast<int64_t>(tn) * BN + et;
+            const bool rok = grow < p.Mk, cok = et < BN && gc < p.Nk;
+            r.rscale = e.scale;
+            r.cscale = 1.0f;
+            r.rbias = 0;
+            r.cbias = 0;
+            if (e.scale_axis == AX_M && rok) r.rscale = e.scales[b * e.scale_bs + grow];
+            if (e.bias_axis == AX_M && rok) r.rbias = e.bias[b * e.bias_bs + grow];
+            if (e.scale_axis == AX_N && cok) r.cscale = e.scales[b * e.scale_bs + gc];
+            if (e.bias_axis == AX_N && cok) r.cbias = e.bias[b * e.bias_bs + gc];
+        };
+        double r_se = 0.0, r_nms = 0.0;
+        uint32_t r_ulo = 0, r_uhi = 0, r_bp = 0x80000000u;
+        auto commit = [&](const Raw& r, int buf) {
+            if (e.scale_axis != AX_N) make_scale_param(r.rscale, r_se, r_nms, r_ulo, r_uhi);
+            r_bp = static_cast<uint32_t>(r.rbias) + 0x80000000u;
+            if (col_params) {
+                if (et < BN) {
+                    ColParam c;
+                    if (e.scale_axis == AX_N) {
+                        make_scale_param(r.cscale, c.se, c.nms, c.ulo, c.uhi);
+                    } else {  // the scale lives in each thread's registers
+                        c.se = 0.0;
+                        c.nms = 0.0;
+                        c.ulo = 0;
+                        c.uhi = 0;
+                    }
+                    c.bias_plus = static_cast<uint32_t>(r.cbias) + 0x80000000u;
+                    c.pad = 0;
+                    cparams[buf * BN + et] = c;
+                }
+                mbar_arrive(&pready[buf]);
+            }
+        };
+
+        Sched sch(p);
+        Work w, wn;
+        bool has = sch.next(p, w);
+        Raw raw;
+        if (C::QUANT && has) {
+            load_raw(w.tile, raw);
+            commit(raw, 0);
+        }
+        for (int local = 0; has; ++local) {
+            const bool has_n = sch.next(p, wn);
+            int b, tm, tn;
+            decode_tile(w.tile, p, b, tm, tn);
             const int acc = local & 1;
             const uint32_t aph = (local >> 1) & 1;
-            const int row = q * 32 + lane;
             const int64_t grow = static_cast<int64_t>(tm) * BM + row;
             const int64_t gcol0 = static_cast<int64_t>(tn) * BN;
             const bool row_ok = grow < p.Mk;
+            const ColParam* cp = cparams + acc * BN;
 
-            // Requant parameters: per-row values in registers, per-column values shared
-            // through shared memory (double-buffered by accumulator, published by pready).
-            double r_se = 0.0, r_nms = 0.0;
-            int r_vlo = 0, r_vhi = 0, r_bias = 0;
-            ColParam* cp = cparams + acc * BN;
-            if constexpr (OUT == Out::Q8) {
-                if (e.scale_axis != AX_N) {
-                    float s = e.scale;
-                    if (e.scale_axis == AX_M)
-                        s = row_ok ? e.scales[b * e.scale_bs + grow] : 1.0f;
-                    make_scale_param(s, r_se, r_nms, r_vlo, r_vhi);
-                }
-                if (e.bias_axis == AX_M && row_ok) r_bias = e.bias[b * e.bias_bs + grow];
-                if (e.scale_axis == AX_N || e.bias_axis == AX_N) {
-                    for (int j = et; j < BN; j += 128) {
-                        const int64_t gc = gcol0 + j;
-                        const bool cok = gc < p.Nk;
-                        ColParam c;
-                        if (e.scale_axis == AX_N) {
-                            make_scale_param(cok ? e.scales[b * e.scale_bs + gc] : 1.0f, c.se,
-                                             c.nms, c.vlo, c.vhi);
-                        } else {  // the scale lives in each thread's registers
-                            c.se = 0.0;
-                            c.nms = 0.0;
-                            c.vlo = 0;
-                            c.vhi = 0;
-                        }
-                        c.bias = (e.bias_axis == AX_N && cok) ? e.bias[b * e.bias_bs + gc] : 0;
-                        c.pad = 0;
-                        cp[j] = c;
-                    }
-                    mbar_arrive(&pready[acc]);
-                    if (!warp_wait(&pready[acc], aph, abort_flag, p.status,
-                                   GK_DEV_TIMEOUT_EPILOGUE, tmo))
-                        break;
-                }
-            }
-
+            if (col_params && !warp_wait(&pready[acc], aph, abort_flag, p.status,
+                                         GK_DEV_TIMEOUT_EPILOGUE, tmo))
+                break;
             if (!warp_wait(&tfull[acc], aph, abort_flag, p.status, GK_DEV_TIMEOUT_EPILOGUE, tmo))
                 break;
             tc_fence_after();
 
+            Raw raw_next;
+            if (C::QUANT && has_n) load_raw(wn.tile, raw_next);
+
             const int64_t obase = static_cast<int64_t>(b) * e.obs + grow * e.ldo;
-#pragma unroll 1
-            for (int c = 0; c < NCHUNK; ++c) {
-                uint32_t v[32];
-                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                                       static_cast<uint32_t>(acc * BN + c * CH);
-                if constexpr (CH == 32)
-                    tmem_ld_x32(taddr, v);
-                else
-                    tmem_ld_x16(taddr, v);
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN + col_base);
+            const bool partial = w.nctr > 1;
+            // stream-K partials of this warp's 32 x WCOLS region: slot j at + j * BM * BN
+            uint32_t* part = nullptr;
+            if (partial)
+                part = p.sk_part +
+                       static_cast<int64_t>(w.tile - p.dp_tiles) * p.sk_maxc * (BM * BN) +
+                       static_cast<int64_t>((warp - 2) * 32 + lane) * C::WCOLS;
+            // Double-buffered TMEM reads: chunk c + 1 is in flight while chunk c is processed.
+            uint32_t va[32], vb[32];
+            tmem_ld_chunk<CH>(tbase, va);
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                uint32_t(&cur)[32] = (c & 1) ? vb : va;
+                uint32_t(&nxt)[32] = (c & 1) ? va : vb;
                 tmem_wait_ld();
-                if (c == NCHUNK - 1) {
+                reg_fence<CH>(cur);
+                if (c + 1 < NCH) {
+                    tmem_ld_chunk<CH>(tbase + (c + 1) * CH, nxt);
+                } else {
                     tc_fence_before();
                     mbar_arrive(&tempty[acc]);
                 }
-                if (!row_ok) continue;
-                const int64_t gc = gcol0 + c * CH;
-                const bool full_chunk = gc + CH <= p.Nk;
-
-                if constexpr (OUT == Out::Q8) {
-                    int r[CH];
-                    if (e.scale_axis == AX_N) {
-                        // per-column scale (and a per-column or per-row bias)
+                if (partial) {
+                    uint32_t* dst = part + static_cast<int64_t>(w.slot) * (BM * BN) + c * CH;
 #pragma unroll
-                        for (int i = 0; i < CH; ++i) {
-                            const ColParam& pc = cp[c * CH + i];
-                            const int bias = e.bias_axis == AX_N ? pc.bias : r_bias;
-                            r[i] = requant_one(static_cast<int32_t>(v[i]), bias, pc.se, pc.nms,
-                                               pc.vlo, pc.vhi, e.zp, e.lo, e.hi);
+                    for (int g = 0; g < CH / 4; ++g)
+                        st_global_v4(dst + 4 * g, cur[4 * g], cur[4 * g + 1], cur[4 * g + 2],
+                                     cur[4 * g + 3]);
+                } else if (row_ok) {
+                    epilogue_chunk<OUT, CH>(cur, p, e, obase, gcol0 + col_base + c * CH,
+                                            cp + col_base + c * CH, r_se, r_nms, r_ulo, r_uhi,
+                                            r_bp);
+                }
+            }
+            if (partial) {
+                // Publish this slot, then count it; the last contributor of the region sums
+                // every slot in slot order (exact for integers, fixed order for floats).
+                __threadfence();
+                __syncwarp();
+                uint32_t last = 0;
+                if (lane == 0) {
+                    uint32_t* ctr = p.sk_ctr + static_cast<int64_t>(w.tile - p.dp_tiles) *
+                                                   C::NEPI + (warp - 2);
+                    uint32_t old = atomicAdd(ctr, 0u);
+                    while (true) {
+                        const uint32_t nv =
+                            (old >> 8) == p.sk_epoch ? old + 1u : ((p.sk_epoch << 8) | 1u);
+                        const uint32_t prev = atomicCAS(ctr, old, nv);
+                        if (prev == old) {
+                            last = (nv & 0xFFu) == static_cast<uint32_t>(w.nctr) ? 1u : 0u;
+                            break;
                         }
-                    } else if (e.bias_axis == AX_N) {
-                        // per-row (or per-tensor) scale in registers, per-column bias
-#pragma unroll
-                        for (int i = 0; i < CH; ++i)
-                            r[i] = requant_one(static_cast<int32_t>(v[i]), cp[c * CH + i].bias,
-                                               r_se, r_nms, r_vlo, r_vhi, e.zp, e.lo, e.hi);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < CH; ++i)
-                            r[i] = requant_one(static_cast<int32_t>(v[i]), r_bias, r_se, r_nms,
-                                               r_vlo, r_vhi, e.zp, e.lo, e.hi);
+                        old = prev;
                     }
-                    uint8_t* out = static_cast<uint8_t*>(e.out);
-                    if (e.vec && full_chunk) {
-                        uint8_t* dst = out + obase + gc;
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+#pragma unroll 1
+                    for (int c = 0; c < NCH; ++c) {
+                        uint32_t sum[32];
 #pragma unroll
-                        for (int g = 0; g < CH / 16; ++g) {
-                            uint32_t w[4];
-#pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                const int* x = r + g * 16 + u * 4;
-                                w[u] = (static_cast<uint32_t>(x[0]) & 0xFFu) |
-                                       ((static_cast<uint32_t>(x[1]) & 0xFFu) << 8) |
-                                       ((static_cast<uint32_t>(x[2]) & 0xFFu) << 16) |
-                                       ((static_cast<uint32_t>(x[3]) & 0xFFu) << 24);
-                            }
-                            st_global_v4(dst + g * 16, w[0], w[1], w[2], w[3]);
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < CH; ++i)
-                            if (gc + i < p.Nk)
-                                out[obase + (gc + i) * e.cso] = static_cast<uint8_t>(r[i]);
-                    }
-                } else if constexpr (OUT == Out::I32) {
-                    int32_t* out = static_cast<int32_t*>(e.out);
-                    uint32_t r[CH];
-                    const uint32_t al = static_cast<uint32_t>(e.alpha_i);
-                    const uint32_t be = static_cast<uint32_t>(e.beta_i);
-                    if (e.vec && full_chunk) {
-                        int32_t* dst = out + obase + gc;
-                        if (be != 0u) {
+                        for (int i = 0; i < CH; ++i) sum[i] = 0u;
+                        for (int j = 0; j < w.nctr; ++j) {
+                            const uint32_t* src = part + static_cast<int64_t>(j) * (BM * BN) + c * CH;
 #pragma unroll
                             for (int g = 0; g < CH / 4; ++g) {
-                                const uint4 cv = ld_global_v4(dst + g * 4);
-                                r[g * 4 + 0] = be * cv.x + al * v[g * 4 + 0];
-                                r[g * 4 + 1] = be * cv.y + al * v[g * 4 + 1];
-                                r[g * 4 + 2] = be * cv.z + al * v[g * 4 + 2];
-                                r[g * 4 + 3] = be * cv.w + al * v[g * 4 + 3];
+                                const uint4 x = __ldcg(reinterpret_cast<const uint4*>(src) + g);
+                                if constexpr (KIND == Kind::I8) {
+                                    sum[4 * g + 0] += x.x;
+                                    sum[4 * g + 1] += x.y;
+                                    sum[4 * g + 2] += x.z;
+                                    sum[4 * g + 3] += x.w;
+                                } else {
+                                    sum[4 * g + 0] = __float_as_uint(__uint_as_float(sum[4 * g + 0]) + __uint_as_float(x.x));
+                                    sum[4 * g + 1] = __float_as_uint(__uint_as_float(sum[4 * g + 1]) + __uint_as_float(x.y));
+                                    sum[4 * g + 2] = __float_as_uint(__uint_as_float(sum[4 * g + 2]) + __uint_as_float(x.z));
+                                    sum[4 * g + 3] = __float_as_uint(__uint_as_float(sum[4 * g + 3]) + __uint_as_float(x.w));
+                                }
                             }
-                        } else {
-#pragma unroll
-                            for (int i = 0; i < CH; ++i) r[i] = al * v[i];
                         }
-#pragma unroll
-                        for (int g = 0; g < CH / 4; ++g)
-                            st_global_v4(dst + g * 4, r[g * 4], r[g * 4 + 1], r[g * 4 + 2],
-                                         r[g * 4 + 3]);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < CH; ++i) {
-                            if (gc + i >= p.Nk) continue;
-                            int32_t* cptr = out + obase + (gc + i) * e.cso;
-                            uint32_t o = al * v[i];
-                            if (be != 0u) o += be * static_cast<uint32_t>(*cptr);
-                            *cptr = static_cast<int32_t>(o);
-                        }
-                    }
-                } else {  // F32
-                    float* out = static_cast<float*>(e.out);
-                    const float al = e.alpha_f, be = e.beta_f;
-                    if (e.vec && full_chunk) {
-                        float* dst = out + obase + gc;
-#pragma unroll
-                        for (int g = 0; g < CH / 4; ++g) {
-                            float x0 = al * __uint_as_float(v[g * 4 + 0]);
-                            float x1 = al * __uint_as_float(v[g * 4 + 1]);
-                            float x2 = al * __uint_as_float(v[g * 4 + 2]);
-                            float x3 = al * __uint_as_float(v[g * 4 + 3]);
-                            if (be != 0.0f) {
-                                const uint4 cv = ld_global_v4(dst + g * 4);
-                                x0 = __fmaf_rn(be, __uint_as_float(cv.x), x0);
-                                x1 = __fmaf_rn(be, __uint_as_float(cv.y), x1);
-                                x2 = __fmaf_rn(be, __uint_as_float(cv.z), x2);
-                                x3 = __fmaf_rn(be, __uint_as_float(cv.w), x3);
-                            }
-                            st_global_v4(dst + g * 4, __float_as_uint(x0), __float_as_uint(x1),
-                                         __float_as_uint(x2), __float_as_uint(x3));
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < CH; ++i) {
-                            if (gc + i >= p.Nk) continue;
-                            float* cptr = out + obase + (gc + i) * e.cso;
-                            float x = al * __uint_as_float(v[i]);
-                            if (be != 0.0f) x = __fmaf_rn(be, *cptr, x);
-                            *cptr = x;
-                        }
+                        if (row_ok)
+                            epilogue_chunk<OUT, CH>(sum, p, e, obase, gcol0 + col_base + c * CH,
+                                                    cp + col_base + c * CH, r_se, r_nms, r_ulo,
+                                                    r_uhi, r_bp);
                     }
                 }
             }
+            if (C::QUANT && has_n) commit(raw_next, acc ^ 1);
+            w = wn;
+            has = has_n;
         }
     }
 
@@ -500,11 +680,15 @@ static PFN_tmapEncodeTiled get_encode() {
 static __device__ unsigned int g_status[64];
 
 unsigned int* device_status_ptr() {
+    static unsigned int* cache[64] = {nullptr};
     int dev = 0;
     cudaGetDevice(&dev);
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return nullptr;
-    return static_cast<unsigned int*>(p) + (dev & 63);
+    if (!cache[dev & 63]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return nullptr;
+        cache[dev & 63] = static_cast<unsigned int*>(p) + (dev & 63);
+    }
+    return cache[dev & 63];
 }
 
 int sm_count() {
@@ -520,8 +704,52 @@ int sm_count() {
     return cache[dev];
 }
 
+// A small per-thread cache of encoded tensor maps: serving loops call the same shapes over
+// the same buffers, and encoding costs about a microsecond per operand.
+struct TmapKey {
+    const void* ptr;
+    int64_t K, rows, ld, bs, batch;
+    int es, box_rows;
+    bool operator==(const TmapKey& o) const {
+        return ptr == o.ptr && K == o.K && rows == o.rows && ld == o.ld && bs == o.bs &&
+               batch == o.batch && es == o.es && box_rows == o.box_rows;
+    }
+};
+struct TmapEntry {
+    TmapKey key;
+    CUtensorMap map;
+    int dev;
+};
+constexpr int TMAP_CACHE = 16;
+thread_local TmapEntry g_tmap_cache[TMAP_CACHE];
+thread_local int g_tmap_used = 0, g_tmap_next = 0;
+
+static int encode_operand_uncached(CUtensorMap* map, const Operand& op, int64_t K, int64_t batch,
+                                   int es, int box_rows, char* err, size_t errlen);
+
 static int encode_operand(CUtensorMap* map, const Operand& op, int64_t K, int64_t batch, int es,
                           int box_rows, char* err, size_t errlen) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const TmapKey key{op.ptr, K, op.rows, op.ld, op.bs, batch, es, box_rows};
+    for (int i = 0; i < g_tmap_used; ++i)
+        if (g_tmap_cache[i].dev == dev && g_tmap_cache[i].key == key) {
+            *map = g_tmap_cache[i].map;
+            return 0;
+        }
+    int rc = encode_operand_uncached(map, op, K, batch, es, box_rows, err, errlen);
+    if (rc) return rc;
+    TmapEntry& e = g_tmap_cache[g_tmap_next];
+    e.key = key;
+    e.map = *map;
+    e.dev = dev;
+    g_tmap_next = (g_tmap_next + 1) % TMAP_CACHE;
+    if (g_tmap_used < TMAP_CACHE) ++g_tmap_used;
+    return 0;
+}
+
+static int encode_operand_uncached(CUtensorMap* map, const Operand& op, int64_t K, int64_t batch,
+                                   int es, int box_rows, char* err, size_t errlen) {
     PFN_tmapEncodeTiled enc = get_encode();
     if (!enc) {
         snprintf(err, errlen, "gemmkit: cuTensorMapEncodeTiled is unavailable (driver too old?)");
@@ -552,7 +780,8 @@ static int encode_operand(CUtensorMap* map, const Operand& op, int64_t K, int64_
 }
 
 template <Kind KIND, Out OUT, int BN>
-static int launch_one(const TcProblem& pr, GemmParams gp, char* err, size_t errlen) {
+static int launch_one(const TcProblem& pr, const TcPlan& plan, GemmParams gp, char* err,
+                      size_t errlen) {
     using C = TileCfg<OUT, BN>;
     constexpr int ES = (KIND == Kind::I8) ? 1 : 2;
     CUtensorMap ta, tb;
@@ -583,11 +812,22 @@ static int launch_one(const TcProblem& pr, GemmParams gp, char* err, size_t errl
         }
         attr_done[dev & 63] = 1;
     }
-    gp.tiles_n = static_cast<int>((pr.Nk + BN - 1) / BN);
+    gp.tiles_n = plan.tiles_n;
     gp.tiles_per_batch = gp.tiles_m * gp.tiles_n;
-    gp.num_tiles = gp.tiles_per_batch * gp.batch;
-    const int grid = gp.num_tiles < sm_count() ? gp.num_tiles : sm_count();
-    kern<<<grid, NTHREADS, C::SMEM, pr.stream>>>(ta, tb, gp);
+    gp.num_tiles = plan.num_tiles;
+    gp.dp_tiles = plan.dp_tiles;
+    gp.sk_iters = plan.sk_iters;
+    gp.sk_maxc = plan.sk_maxc;
+    if (plan.sk_iters > 0) {
+        if (!pr.sk_part || !pr.sk_ctr) {
+            snprintf(err, errlen, "gemmkit: internal error: stream-K plan without scratch");
+            return 1;
+        }
+        gp.sk_part = pr.sk_part;
+        gp.sk_ctr = pr.sk_ctr;
+        gp.sk_epoch = pr.sk_epoch & 0xFFFFFFu;
+    }
+    kern<<<plan.grid, C::THREADS, C::SMEM, pr.stream>>>(ta, tb, gp);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         snprintf(err, errlen, "gemmkit: kernel launch failed: %s", cudaGetErrorString(e));
@@ -614,47 +854,87 @@ static int pick_bn(const TcProblem& p) {
     return 64;
 }
 
+void plan_tc_gemm(const TcProblem& p, bool allow_sk, TcPlan* plan) {
+    TcPlan& pl = *plan;
+    memset(&pl, 0, sizeof(pl));
+    pl.bn = pick_bn(p);
+    pl.nepi = pl.bn >= 64 ? 8 : 4;
+    pl.tiles_m = static_cast<int>((p.Mk + BM - 1) / BM);
+    pl.tiles_n = static_cast<int>((p.Nk + pl.bn - 1) / pl.bn);
+    pl.num_tiles = pl.tiles_m * pl.tiles_n * static_cast<int>(p.batch);
+    const int es = p.kind == Kind::I8 ? 1 : 2;
+    pl.num_kb = static_cast<int>((p.K * es + BKB - 1) / BKB);
+    const int sms = sm_count();
+    pl.grid = pl.num_tiles < sms ? pl.num_tiles : sms;
+    pl.dp_tiles = pl.num_tiles;
+    // Stream-K tail: when the last wave of whole tiles would leave SMs idle, spread the K
+    // blocks of that wave's tiles over every SM (needs >= 4 K blocks per tile to pay off).
+    const int rem = pl.num_tiles % sms;
+    if (allow_sk && pl.num_kb >= 4 && rem != 0) {
+        const int sk_tiles = pl.num_tiles < sms ? pl.num_tiles : rem;
+        const int64_t iters = static_cast<int64_t>(sk_tiles) * pl.num_kb;
+        if (iters >= sms) {
+            const int64_t per = iters / sms;  // >= 1
+            const int64_t maxc = (pl.num_kb + per - 1) / per + 1;
+            if (maxc <= 255) {
+                pl.dp_tiles = pl.num_tiles - sk_tiles;
+                pl.sk_iters = iters;
+                pl.sk_maxc = static_cast<int>(maxc);
+                pl.grid = sms;
+                pl.part_words = static_cast<int64_t>(sk_tiles) * maxc * BM * pl.bn;
+                pl.ctr_words = static_cast<int64_t>(sk_tiles) * pl.nepi;
+            }
+        }
+    }
+}
+
 template <Kind KIND, Out OUT>
-static int dispatch_bn(const TcProblem& pr, const GemmParams& gp, int bn, char* err,
+static int dispatch_bn(const TcProblem& pr, const TcPlan& plan, const GemmParams& gp, char* err,
                        size_t errlen) {
-    switch (bn) {
-        case 16: return launch_one<KIND, OUT, 16>(pr, gp, err, errlen);
-        case 32: return launch_one<KIND, OUT, 32>(pr, gp, err, errlen);
-        case 64: return launch_one<KIND, OUT, 64>(pr, gp, err, errlen);
-        case 128: return launch_one<KIND, OUT, 128>(pr, gp, err, errlen);
-        case 256: return launch_one<KIND, OUT, 256>(pr, gp, err, errlen);
+    switch (plan.bn) {
+        case 16: return launch_one<KIND, OUT, 16>(pr, plan, gp, err, errlen);
+        case 32: return launch_one<KIND, OUT, 32>(pr, plan, gp, err, errlen);
+        case 64: return launch_one<KIND, OUT, 64>(pr, plan, gp, err, errlen);
+        case 128: return launch_one<KIND, OUT, 128>(pr, plan, gp, err, errlen);
+        case 256: return launch_one<KIND, OUT, 256>(pr, plan, gp, err, errlen);
         default:
-            snprintf(err, errlen, "gemmkit: unsupported tile width %d", bn);
+            snprintf(err, errlen, "gemmkit: unsupported tile width %d", plan.bn);
             return 1;
     }
 }
 
-int launch_tc_gemm(const TcProblem& pr, char* err, size_t errlen) {
+int launch_tc_gemm_planned(const TcProblem& pr, const TcPlan& plan, char* err, size_t errlen) {
     GemmParams gp;
     memset(&gp, 0, sizeof(gp));
     gp.Mk = pr.Mk;
     gp.Nk = pr.Nk;
     gp.K = static_cast<int32_t>(pr.K);
     gp.batch = static_cast<int32_t>(pr.batch);
-    gp.tiles_m = static_cast<int>((pr.Mk + BM - 1) / BM);
-    const int es = pr.kind == Kind::I8 ? 1 : 2;
-    gp.num_kb = static_cast<int>((pr.K * es + BKB - 1) / BKB);
+    gp.tiles_m = plan.tiles_m;
+    gp.num_kb = plan.num_kb;
     gp.group_m = 16;
     gp.a_batched = pr.a.bs != 0 && pr.batch > 1;
     gp.b_batched = pr.b.bs != 0 && pr.batch > 1;
     gp.timeout_ns = 4000000000ull;
     gp.status = device_status_ptr();
     gp.e = pr.e;
-    const int bn = pick_bn(pr);
     if (pr.kind == Kind::I8) {
-        if (pr.out == Out::I32) return dispatch_bn<Kind::I8, Out::I32>(pr, gp, bn, err, errlen);
-        if (pr.out == Out::Q8) return dispatch_bn<Kind::I8, Out::Q8>(pr, gp, bn, err, errlen);
+        if (pr.out == Out::I32) return dispatch_bn<Kind::I8, Out::I32>(pr, plan, gp, err, errlen);
+        if (pr.out == Out::Q8) return dispatch_bn<Kind::I8, Out::Q8>(pr, plan, gp, err, errlen);
+        if (pr.out == Out::U8) return dispatch_bn<Kind::I8, Out::U8>(pr, plan, gp, err, errlen);
     } else if (pr.out == Out::F32) {
-        if (pr.kind == Kind::BF16) return dispatch_bn<Kind::BF16, Out::F32>(pr, gp, bn, err, errlen);
-        return dispatch_bn<Kind::F16, Out::F32>(pr, gp, bn, err, errlen);
+        if (pr.kind == Kind::BF16)
+            return dispatch_bn<Kind::BF16, Out::F32>(pr, plan, gp, err, errlen);
+        return dispatch_bn<Kind::F16, Out::F32>(pr, plan, gp, err, errlen);
     }
     snprintf(err, errlen, "gemmkit: internal error: unsupported kernel combination");
     return 1;
+}
+
+int launch_tc_gemm(const TcProblem& pr, char* err, size_t errlen) {
+    TcPlan plan;
+    plan_tc_gemm(pr, false, &plan);
+    return launch_tc_gemm_planned(pr, plan, err, errlen);
 }
 
 }  // namespace gk

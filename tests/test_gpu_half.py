@@ -118,3 +118,23 @@ def test_half_degenerate():
     dc = dev(np.arange(6, dtype=np.float32))
     gk.gemm_bf16_f32_unchecked(2, 0, 3, 1.0, 0, 0, 1, 0, 3, 1, 2.0, dc.data_ptr(), 3, 1)
     assert host(dc).tolist() == [0.0, 2.0, 4.0, 6.0, 8.0, 10.0]
+
+
+@pytest.mark.parametrize("shape", [(1000, 1000, 1000), (3000, 640, 700)])
+def test_half_stream_k_beta(shape):
+    """bf16 shapes with a stream-K tail: f32 partials summed in slot order, beta once."""
+    m, k, n = shape
+    rng = np.random.default_rng(m + n)
+    a = make(rng, (m, k), False)
+    b = make(rng, (k, n), False)
+    c0 = rng.standard_normal((m, n)).astype(np.float32)
+    da, db = dev(a.view(np.int16)), dev(np.ascontiguousarray(b.T).view(np.int16))
+    outs = []
+    for _ in range(2):
+        dc = dev(c0)
+        gk.gemm_half_f32(1.5, gk.MatRef.from_row_major(da, m, k), gk.MatRef.new(db, k, n, 1, k),
+                         0.5, gk.MatMut.from_row_major(dc, m, n))
+        outs.append(host(dc).reshape(m, n))
+    assert np.array_equal(outs[0], outs[1])  # deterministic reduction order
+    rows = np.arange(0, m, 37)
+    check(outs[0], a, b, 1.5, 0.5, c0, False, rows=rows)

@@ -406,3 +406,63 @@ def test_general_strided_views():
                                     3, 3 * m)
     got = gather(host(dc), m, n, 3, 3 * m)
     assert np.array_equal(got, want)
+
+
+# ---- stream-K tail (tiles cut between CTAs, partials summed by the last arriver) ---------------
+
+SK_SHAPES = [(1000, 1000, 1000), (700, 2000, 300), (2048, 2048, 2304), (16, 4096, 14336 // 4)]
+
+
+@pytest.mark.parametrize("shape", SK_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_stream_k_i32_beta(shape):
+    """Shapes whose last wave is split over all SMs (K blocks >= 4); beta != 0 is applied once,
+    by the CTA that finishes each region. Three calls in a row exercise the counter epochs."""
+    m, k, n = shape
+    rng = np.random.default_rng(m + k + n)
+    a = rand_i8(rng, (m, k))
+    bT = rand_i8(rng, (n, k))
+    c0 = rng.integers(-1000, 1000, (m, n)).astype(np.int32)
+    want = O.gemm_i8_matrix(3, a, bT.T, -2, c0)
+    da, db = dev(a), dev(bT)
+    for _ in range(3):
+        dc = dev(c0)
+        gk.gemm_i8(3, gk.MatRef.from_row_major(da, m, k), gk.MatRef.new(db, k, n, 1, k), -2,
+                   gk.MatMut.from_row_major(dc, m, n))
+        assert np.array_equal(host(dc).reshape(m, n), want)
+
+
+@pytest.mark.parametrize("out_u8", [False, True])
+@pytest.mark.parametrize("shape", SK_SHAPES[:3], ids=lambda s: "x".join(map(str, s)))
+def test_stream_k_requant(shape, out_u8):
+    m, k, n = shape
+    rng = np.random.default_rng(m * 3 + k + n)
+    a = rand_i8(rng, (m, k), -127, 127)
+    bT = rand_i8(rng, (n, k), -127, 127)
+    bias = rng.integers(-2**15, 2**15 + 1, n).astype(np.int32)
+    scales = rng.uniform(1e-4, 1e-3, m).astype(np.float32)
+    zp = 100 if out_u8 else -7
+    want = O.requant_matrix(a, bT.T, scales=scales, scale_axis="row", bias=bias, bias_axis="col",
+                            zp=zp, out_u8=out_u8, relu=True)
+    da, db, dbias, dsc = dev(a), dev(bT), dev(bias), dev(scales)
+    req = gk.Requantize(gk.RequantScale.PerRow(dsc), zp, dbias, gk.AXIS_COL, True)
+    for _ in range(2):
+        dc = empty(m * n, np.uint8 if out_u8 else np.int8)
+        gk.gemm_i8_requant_ex_unchecked(m, k, n, ptr(da), k, 1, ptr(db), 1, k, req, ptr(dc), n, 1,
+                                        out_u8=out_u8)
+        assert np.array_equal(host(dc).reshape(m, n), want)
+
+
+def test_stream_k_prepacked_gemv_sizes():
+    """Small-M over a prepacked B of several widths (112, 50 and 7 row tiles)."""
+    rng = np.random.default_rng(77)
+    for (M, k, n) in [(4, 4096, 14336), (9, 1024, 6400), (1, 8192, 896)]:
+        a = rand_i8(rng, (M, k), -127, 127)
+        bT = rand_i8(rng, (n, k), -127, 127)
+        scales = rng.uniform(1e-4, 1e-3, n).astype(np.float32)
+        want = O.requant_matrix(a, bT.T, scales=scales, scale_axis="col", zp=3)
+        da, dbT, dsc = dev(a), dev(bT), dev(scales)
+        packed = gk.prepack_rhs_i8(gk.MatRef.new(dbT, k, n, 1, k))
+        dc = empty(M * n, np.int8)
+        gk.gemm_i8_packed_b_requant(M, ptr(da), k, 1, packed, gk.Requantize(
+            gk.RequantScale.PerCol(dsc), 3), ptr(dc), n, 1)
+        assert np.array_equal(host(dc).reshape(M, n), want), (M, k, n)
