@@ -85,13 +85,23 @@ bool streamk_enabled() {
     return env == 1;
 }
 
+// GEMMKIT_CUDA_PAIR=0 disables the CTA-pair (cta_group::2) kernel for large tiles.
+bool pair_enabled() {
+    static int env = -1;
+    if (env == -1) {
+        const char* s = getenv("GEMMKIT_CUDA_PAIR");
+        env = (s && s[0] == '0') ? 0 : 1;
+    }
+    return env == 1;
+}
+
 int tile_n_override() {
     if (g_tile_n >= 0) return g_tile_n;
     static int env = -2;
     if (env == -2) {
         const char* s = getenv("GEMMKIT_CUDA_BN");
         int v = s ? atoi(s) : 0;
-        env = (v == 16 || v == 32 || v == 64 || v == 128 || v == 256) ? v : 0;
+        env = (v == 16 || v == 32 || v == 64 || v == 128 || v == 192 || v == 256) ? v : 0;
     }
     return env;
 }
@@ -457,7 +467,7 @@ int execute(const Job& j) {
     pr.bn = tile_n_override();
     pr.stream = j.stream;
     gk::TcPlan plan;
-    gk::plan_tc_gemm(pr, streamk_enabled(), &plan);
+    gk::plan_tc_gemm2(pr, streamk_enabled(), pair_enabled(), &plan);
     const int64_t part_bytes = round_up(plan.part_words * 4, 256);
 
     gk_workspace* ws = j.ws ? j.ws : default_ws(dev);
@@ -580,8 +590,8 @@ void gk_workspace_free(gk_workspace* ws) {
 }
 
 int gk_set_tile_n(int bn) {
-    if (!(bn == 0 || bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 256))
-        return set_err(GK_EINVAL, "gemmkit: tile width must be 0, 16, 32, 64, 128 or 256");
+    if (!(bn == 0 || bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 192 || bn == 256))
+        return set_err(GK_EINVAL, "gemmkit: tile width must be 0, 16, 32, 64, 128, 192 or 256");
     g_tile_n = bn;
     return GK_OK;
 }

@@ -91,6 +91,7 @@ struct TcProblem {
 // Launch geometry chosen for a problem (tile width, grid, stream-K split and the scratch it
 // needs). plan_tc_gemm fills it; allow_sk = false plans without a stream-K tail.
 struct TcPlan {
+    int pair;  // 1: CTA-pair kernel (256-row tiles over two SMs, cluster of 2)
     int bn, nepi, tiles_m, tiles_n, num_tiles, num_kb, grid;
     int dp_tiles, sk_maxc;
     int64_t sk_iters;
@@ -98,6 +99,11 @@ struct TcPlan {
     int64_t ctr_words;   // 32-bit words of sk_ctr
 };
 void plan_tc_gemm(const TcProblem& p, bool allow_sk, TcPlan* plan);
+// allow_pair enables the CTA-pair kernel where it applies (GEMMKIT_CUDA_PAIR knob).
+void plan_tc_gemm2(const TcProblem& p, bool allow_sk, bool allow_pair, TcPlan* plan);
+struct GemmParams;
+int launch_pair(const TcProblem& pr, const TcPlan& plan, const GemmParams& gp, char* err,
+                size_t errlen);
 int launch_tc_gemm_planned(const TcProblem& p, const TcPlan& plan, char* err, size_t errlen);
 
 // Launch the tcgen05 GEMM for `p` (all operands already TMA-compatible). Returns a GK_*

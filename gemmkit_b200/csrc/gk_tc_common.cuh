@@ -1,0 +1,269 @@
+// gk_tc_common.cuh -- device pieces shared by the one-CTA and the CTA-pair tensor-core GEMM
+// kernels: tile constants, the exact requant arithmetic, saturating packs, the tile order,
+// the work schedule, and the per-chunk epilogue.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gk_engine.h"
+#include "gk_sm100.cuh"
+
+namespace gk {
+
+constexpr int BM = 128;     // MMA M (TMEM lanes)
+constexpr int BKB = 128;    // bytes of K per stage and row (one 128-byte swizzle atom)
+constexpr int MMA_KB = 32;  // bytes of K per tcgen05.mma (kind::i8 K=32, kind::f16 K=16)
+constexpr int SMEM_LIMIT = 232448;
+
+// Per-scale constants of the exact requant (see requant_q).
+struct alignas(16) ColParam {
+    double se;           // min(scale, 2048), exact
+    double nms;          // -(2^52 + 2^31) * se, exact (22-bit x 24-bit significands)
+    uint32_t ulo, uhi;   // accumulator clamp [vlo, vhi], offset by 2^31 (unsigned domain)
+    uint32_t bias_plus;  // bias + 2^31 (mod 2^32)
+    uint32_t pad;
+};
+
+__device__ __forceinline__ void make_scale_param(float s, double& se, double& nms, uint32_t& ulo,
+                                                 uint32_t& uhi) {
+    const double s64 = static_cast<double>(s);
+    se = s64 < 2048.0 ? s64 : 2048.0;
+    nms = -(4503601774854144.0 * se);
+    const double vs = ceil(2048.0 / se) + 1.0;
+    const int vhi = vs >= 2147483647.0 ? 2147483647 : static_cast<int>(vs);
+    const int vlo = vhi == 2147483647 ? (-2147483647 - 1) : -vhi - 1;
+    ulo = static_cast<uint32_t>(vlo) + 0x80000000u;
+    uhi = static_cast<uint32_t>(vhi) + 0x80000000u;
+}
+
+// zp + rne(fl64(f64(v) * f64(scale))) for v = acc +wrap bias, exactly (the caller clamps to
+// the output band). gemmkit's KRequantize::apply (gemmkit/src/kernel/epilogue.rs:810-830):
+//  1. u = acc + bias + 2^31 (mod 2^32) is v + 2^31 as an unsigned number, so the unsigned clamp
+//     to [vlo, vhi] + 2^31 is the signed clamp of v. The map is monotone in v (scale > 0), and
+//     |v| beyond vhi ~ 2048/scale already drives |v*scale| >= 2048, past any clamp band, so the
+//     clamp changes no result; it bounds |v*se| <= 2048 + 3*se <= 8192. For scale > 2048 the
+//     band is v in [-3, 2] with se = 2048 and every v != 0 still saturates, as with scale.
+//  2. d = 2^52 + u = 2^52 + 2^31 + v is exact (built from bits); fma(d, se, -(2^52+2^31)*se)
+//     has the exact value v*se and rounds once: the reference's f64 product fl64(v*scale).
+//  3. p + 1.5*2^52 rounds p to the nearest integer, ties to even (the reference's 2^52 trick,
+//     gemmkit/src/kernel/epilogue.rs:886-897); |p| <= 8192 leaves the integer in the low word.
+//     zp joins after rounding, in integer.
+__device__ __forceinline__ int requant_q(uint32_t acc, uint32_t bias_plus, double se, double nms,
+                                         uint32_t ulo, uint32_t uhi, int zp) {
+    uint32_t u = acc + bias_plus;
+    u = min(max(u, ulo), uhi);
+    const double d = __hiloint2double(0x43300000, static_cast<int>(u));
+    const double p = __fma_rn(d, se, nms);
+    const double y = __dadd_rn(p, 6755399441055744.0);
+    return __double2loint(y) + zp;
+}
+
+// Four values saturated to the output band and packed little-endian (x0 in the low byte).
+template <bool U8>
+__device__ __forceinline__ uint32_t pack4_sat(int x0, int x1, int x2, int x3) {
+    uint32_t t, d;
+    if constexpr (U8) {
+        asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(t) : "r"(x3), "r"(x2), "r"(0));
+        asm("cvt.pack.sat.u8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(x1), "r"(x0), "r"(t));
+    } else {
+        asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(t) : "r"(x3), "r"(x2), "r"(0));
+        asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(x1), "r"(x0), "r"(t));
+    }
+    return d;
+}
+
+__device__ __forceinline__ void decode_tile(int t, const GemmParams& p, int& b, int& tm,
+                                            int& tn) {
+    b = t / p.tiles_per_batch;
+    const int r = t - b * p.tiles_per_batch;
+    const int band_tiles = p.group_m * p.tiles_n;
+    const int band = r / band_tiles;
+    const int first_m = band * p.group_m;
+    const int gsize = min(p.tiles_m - first_m, p.group_m);
+    const int rr = r - band * band_tiles;
+    tm = first_m + rr % gsize;
+    tn = rr / gsize;
+}
+
+// One unit of a CTA's work: K blocks [k0, k1) of `tile`. nctr > 1 marks a stream-K tile cut
+// between nctr CTAs; this CTA holds partial slot `slot` of it.
+struct Work {
+    int tile, k0, k1, slot, nctr;
+};
+
+// The CTA's sequence of work items, computed identically by every role: first the whole tiles
+// blockIdx.x, blockIdx.x + grid, ... below dp_tiles, then this CTA's contiguous share
+// [start(c), start(c + 1)) of the stream-K iterations (sk_iters >= grid, so every share is
+// non-empty and a tile's contributors are consecutive CTAs).
+struct Sched {
+    int cta, G, dp_next;
+    int64_t it, it_end;
+
+    __device__ __forceinline__ explicit Sched(const GemmParams& p) {
+        cta = blockIdx.x;
+        G = gridDim.x;
+        dp_next = cta;
+        it = p.sk_iters > 0 ? start(p, cta) : 0;
+        it_end = p.sk_iters > 0 ? start(p, cta + 1) : 0;
+    }
+    __device__ __forceinline__ int64_t start(const GemmParams& p, int c) const {
+        return (static_cast<int64_t>(c) * p.sk_iters) / G;
+    }
+    // the CTA whose share holds iteration T: the largest c with start(c) <= T
+    __device__ __forceinline__ int owner(const GemmParams& p, int64_t T) const {
+        const int64_t c = ((T + 1) * G + p.sk_iters - 1) / p.sk_iters - 1;
+        return static_cast<int>(c < 0 ? 0 : (c >= G ? G - 1 : c));
+    }
+    __device__ __forceinline__ bool next(const GemmParams& p, Work& w) {
+        if (dp_next < p.dp_tiles) {
+            w = Work{dp_next, 0, p.num_kb, 0, 1};
+            dp_next += G;
+            return true;
+        }
+        if (it < it_end) {
+            const int skt = static_cast<int>(it / p.num_kb);
+            const int k0 = static_cast<int>(it - static_cast<int64_t>(skt) * p.num_kb);
+            const int64_t left = it_end - it;
+            const int k1 = left < p.num_kb - k0 ? k0 + static_cast<int>(left) : p.num_kb;
+            const int64_t T0 = static_cast<int64_t>(skt) * p.num_kb;
+            const int cf = owner(p, T0), cl = owner(p, T0 + p.num_kb - 1);
+            w = Work{p.dp_tiles + skt, k0, k1, cta - cf, cl - cf + 1};
+            it += k1 - k0;
+            return true;
+        }
+        return false;
+    }
+};
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned int* status, unsigned int where,
+                                          uint64_t timeout) {
+    const bool ok = mbar_wait(bar, parity, abort_flag, status, where, timeout);
+    return !__any_sync(0xffffffffu, !ok);
+}
+
+// The epilogue of one chunk of CH accumulator columns held by this thread (its row `grow`),
+// starting at column gc of the output.
+template <Out OUT, int CH>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], const GemmParams& p,
+                                               const EpiParams& e, int64_t obase, int64_t gc,
+                                               const ColParam* cp, double r_se, double r_nms,
+                                               uint32_t r_ulo, uint32_t r_uhi, uint32_t r_bp) {
+    const bool full_chunk = gc + CH <= p.Nk;
+    if constexpr (OUT == Out::Q8 || OUT == Out::U8) {
+        constexpr bool U8 = OUT == Out::U8;
+        int q[CH];
+        if (e.scale_axis == AX_N) {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) {
+                const ColParam& pc = cp[i];
+                const uint32_t bp = e.bias_axis == AX_N ? pc.bias_plus : r_bp;
+                q[i] = requant_q(v[i], bp, pc.se, pc.nms, pc.ulo, pc.uhi, e.zp);
+            }
+        } else if (e.bias_axis == AX_N) {
+#pragma unroll
+            for (int i = 0; i < CH; ++i)
+                q[i] = requant_q(v[i], cp[i].bias_plus, r_se, r_nms, r_ulo, r_uhi, e.zp);
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i)
+                q[i] = requant_q(v[i], r_bp, r_se, r_nms, r_ulo, r_uhi, e.zp);
+        }
+        if (e.relu) {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) q[i] = max(q[i], e.lo);
+        }
+        uint32_t w[CH / 4];
+#pragma unroll
+        for (int g = 0; g < CH / 4; ++g)
+            w[g] = pack4_sat<U8>(q[4 * g], q[4 * g + 1], q[4 * g + 2], q[4 * g + 3]);
+        uint8_t* out = static_cast<uint8_t*>(e.out);
+        if (e.vec && full_chunk) {
+            uint8_t* dst = out + obase + gc;
+#pragma unroll
+            for (int g = 0; g < CH / 16; ++g)
+                st_global_v4(dst + g * 16, w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i)
+                if (gc + i < p.Nk)
+                    out[obase + (gc + i) * e.cso] = static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3)));
+        }
+    } else if constexpr (OUT == Out::I32) {
+        int32_t* out = static_cast<int32_t*>(e.out);
+        uint32_t r[CH];
+        const uint32_t al = static_cast<uint32_t>(e.alpha_i);
+        const uint32_t be = static_cast<uint32_t>(e.beta_i);
+        if (e.vec && full_chunk) {
+            int32_t* dst = out + obase + gc;
+            if (be != 0u) {
+#pragma unroll
+                for (int g = 0; g < CH / 4; ++g) {
+                    const uint4 cv = ld_global_v4(dst + g * 4);
+                    r[g * 4 + 0] = be * cv.x + al * v[g * 4 + 0];
+                    r[g * 4 + 1] = be * cv.y + al * v[g * 4 + 1];
+                    r[g * 4 + 2] = be * cv.z + al * v[g * 4 + 2];
+                    r[g * 4 + 3] = be * cv.w + al * v[g * 4 + 3];
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < CH; ++i) r[i] = al * v[i];
+            }
+#pragma unroll
+            for (int g = 0; g < CH / 4; ++g)
+                st_global_v4(dst + g * 4, r[g * 4], r[g * 4 + 1], r[g * 4 + 2], r[g * 4 + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) {
+                if (gc + i >= p.Nk) continue;
+                int32_t* cptr = out + obase + (gc + i) * e.cso;
+                uint32_t o = al * v[i];
+                if (be != 0u) o += be * static_cast<uint32_t>(*cptr);
+                *cptr = static_cast<int32_t>(o);
+            }
+        }
+    } else {  // F32
+        float* out = static_cast<float*>(e.out);
+        const float al = e.alpha_f, be = e.beta_f;
+        if (e.vec && full_chunk) {
+            float* dst = out + obase + gc;
+#pragma unroll
+            for (int g = 0; g < CH / 4; ++g) {
+                float x0 = al * __uint_as_float(v[g * 4 + 0]);
+                float x1 = al * __uint_as_float(v[g * 4 + 1]);
+                float x2 = al * __uint_as_float(v[g * 4 + 2]);
+                float x3 = al * __uint_as_float(v[g * 4 + 3]);
+                if (be != 0.0f) {
+                    const uint4 cv = ld_global_v4(dst + g * 4);
+                    x0 = __fmaf_rn(be, __uint_as_float(cv.x), x0);
+                    x1 = __fmaf_rn(be, __uint_as_float(cv.y), x1);
+                    x2 = __fmaf_rn(be, __uint_as_float(cv.z), x2);
+                    x3 = __fmaf_rn(be, __uint_as_float(cv.w), x3);
+                }
+                st_global_v4(dst + g * 4, __float_as_uint(x0), __float_as_uint(x1),
+                             __float_as_uint(x2), __float_as_uint(x3));
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) {
+                if (gc + i >= p.Nk) continue;
+                float* cptr = out + obase + (gc + i) * e.cso;
+                float x = al * __uint_as_float(v[i]);
+                if (be != 0.0f) x = __fmaf_rn(be, *cptr, x);
+                *cptr = x;
+            }
+        }
+    }
+}
+
+// Host helpers shared by the launchers (gk_tc_gemm.cu).
+int encode_operand(CUtensorMap* map, const Operand& op, int64_t K, int64_t batch, int es,
+                   int box_rows, char* err, size_t errlen);
+// Tensor map over the tiled prepacked layout (Operand::slab): 128-byte rows already in
+// swizzled order, so the map itself does not swizzle; box = box_rows rows of one K block.
+int encode_tiled_operand(CUtensorMap* map, const Operand& op, int64_t K, int box_rows, char* err,
+                         size_t errlen);
+
+}  // namespace gk

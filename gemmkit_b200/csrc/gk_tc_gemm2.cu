@@ -1,0 +1,449 @@
+// gk_tc_gemm2.cu -- the CTA-pair form of the tensor-core GEMM (tcgen05 cta_group::2).
+//
+// Two CTAs of a cluster on two SMs compute one 256 x BN tile: each loads its own 128 rows of A
+// and its half (BN/2 rows) of B into its shared memory; the even CTA (the leader) issues
+// tcgen05.mma.cta_group::2 with M = 256, which reads A and B from both CTAs' shared memory at
+// the same offsets and leaves each CTA's 128 accumulator rows in its own TMEM. Per MAC this
+// moves a third less operand data into each SM than the one-CTA 128 x BN tile.
+//
+// Synchronisation across the pair (all waits bounded, as in the one-CTA kernel):
+//   full[s]    leader's barrier; both producers arrive with their byte counts and both CTAs'
+//              TMA loads complete on it (cta_group::2 loads may signal the peer's barrier);
+//   empty[s]   one per CTA; the leader's MMA thread commits to both when the stage is read;
+//   tfull[a]   one per CTA; the leader's MMA thread commits to both when a tile is done;
+//   tempty[a]  leader's; every epilogue warp of both CTAs arrives once it has read the tile.
+// A cluster barrier after set-up and before teardown keeps either CTA from touching the
+// other's barriers before they exist or after it has exited.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "gk_engine.h"
+#include "gk_sm100.cuh"
+#include "gk_tc_common.cuh"
+
+namespace gk {
+
+template <Out OUT, int BN>
+struct PairCfg {
+    static constexpr int NEPI = 8;                  // epilogue warps per CTA
+    static constexpr int THREADS = 64 + 32 * NEPI;
+    static constexpr int WCOLS = BN / 2;            // accumulator columns per epilogue warp
+    static constexpr int CH = 32;
+    static constexpr int NCH = WCOLS / CH;
+    static constexpr int A_BYTES = BM * BKB;        // this CTA's 128 rows of A
+    static constexpr int B_BYTES = (BN / 2) * BKB;  // this CTA's half of B
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr bool QUANT = (OUT == Out::Q8 || OUT == Out::U8);
+    static constexpr int CP_BYTES = QUANT ? 2 * BN * 32 : 0;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int RAW_STAGES = (SMEM_LIMIT - 1024 - BAR_BYTES - CP_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES = RAW_STAGES > 10 ? 10 : RAW_STAGES;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + CP_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static_assert(BN == 128 || BN == 256, "pair tile width");
+    static_assert(STAGES >= 2 && SMEM <= SMEM_LIMIT, "shared memory budget");
+    static_assert(2 * STAGES + 7 <= BAR_BYTES / 8 - 1, "barrier area");
+};
+
+template <Kind KIND, Out OUT, int BN>
+__global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+    using C = PairCfg<OUT, BN>;
+    constexpr int STAGES = C::STAGES;
+    constexpr int CH = C::CH;
+    constexpr int NCH = C::NCH;
+    constexpr int NEPI_T = 32 * C::NEPI;
+    constexpr int ES = (KIND == Kind::I8) ? 1 : 2;
+    constexpr int BKE = BKB / ES;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * C::A_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + STAGES;
+    uint64_t* tfull = bars + 2 * STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* pready = tfull + 4;
+    uint64_t* drain = tfull + 6;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 7);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    ColParam* cparams = reinterpret_cast<ColParam*>(smem + STAGES * C::STAGE_BYTES + C::BAR_BYTES);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = static_cast<int>(blockIdx.x >> 1);
+    const int npairs = static_cast<int>(gridDim.x >> 1);
+    const uint64_t tmo = p.timeout_ns;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);  // the leader's producer; the peer's copies only add bytes
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 2 * C::NEPI);  // every epilogue warp of both CTAs
+            mbar_init(&pready[a], NEPI_T);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    // shared::cluster addresses of the barriers that cross the pair
+    const uint32_t full_l = mapa_shared(smem_u32(&full[0]), 0);      // leader's full[0]
+    const uint32_t tempty_l = mapa_shared(smem_u32(&tempty[0]), 0);  // leader's tempty[0]
+    const uint32_t empty_own = mapa_shared(smem_u32(&empty[0]), rank);
+    const uint32_t empty_peer = mapa_shared(smem_u32(&empty[0]), rank ^ 1u);
+    const uint32_t tfull_own = mapa_shared(smem_u32(&tfull[0]), rank);
+    const uint32_t tfull_peer = mapa_shared(smem_u32(&tfull[0]), rank ^ 1u);
+    const uint32_t drain_own = mapa_shared(smem_u32(drain), rank);
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs) ----------------
+            int stage = 0;
+            uint32_t phase = 0, issued = 0, last_par = 0;
+            bool ok = true;
+            for (int t = pair; t < p.num_tiles && ok; t += npairs) {
+                int b, tm, tn;
+                decode_tile(t, p, b, tm, tn);
+                const int za = p.a_batched ? b : 0, zb = p.b_batched ? b : 0;
+                const int arow = tm * 2 * BM + static_cast<int>(rank) * BM;
+                const int brow = tn * BN + static_cast<int>(rank) * (BN / 2);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status,
+                                   GK_DEV_TIMEOUT_PRODUCER, tmo)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = full_l + 8u * stage;
+                    // One local arrival expecting both CTAs' bytes. The peer's copies may land
+                    // first: the transaction count goes negative until this arrival, and the
+                    // phase cannot complete before it. (A cluster-scope release arrival per
+                    // stage from each CTA serialised the ring behind the previous copies.)
+                    if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+                    if (p.a_tiled)
+                        tma_load_3d_pair(sA + stage * C::A_BYTES, &tmA, fb, 0, arow, kb);
+                    else
+                        tma_load_3d_pair(sA + stage * C::A_BYTES, &tmA, fb, kb * BKE, arow, za);
+                    if (p.b_tiled)
+                        tma_load_3d_pair(sB + stage * C::B_BYTES, &tmB, fb, 0, brow, kb);
+                    else
+                        tma_load_3d_pair(sB + stage * C::B_BYTES, &tmB, fb, kb * BKE, brow, zb);
+                    issued |= 1u << stage;
+                    last_par = (last_par & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Drain (leader): its full barriers count both CTAs' copies.
+            if (leader) {
+                int dummy = 0;
+                for (int s = 0; s < STAGES; ++s)
+                    if (issued & (1u << s))
+                        mbar_wait(&full[s], (last_par >> s) & 1u, &dummy, p.status,
+                                  GK_DEV_TIMEOUT_DRAIN, tmo);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // ---------------- MMA issuer (leader) ----------------
+            uint32_t idesc;
+            if constexpr (KIND == Kind::I8)
+                idesc = idesc_i8(2 * BM, BN);
+            else
+                idesc = idesc_f16(2 * BM, BN, KIND == Kind::BF16);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int local = 0;
+            for (int t = pair; t < p.num_tiles && ok; t += npairs, ++local) {
+                const int acc = local & 1;
+                const uint32_t aph = (local >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, p.status, GK_DEV_TIMEOUT_MMA,
+                               tmo)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.status, GK_DEV_TIMEOUT_MMA,
+                                   tmo)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+                    for (int ks = 0; ks < BKB / MMA_KB; ++ks) {
+                        const uint64_t ad = sdesc_kmajor_sw128(a0 + ks * MMA_KB);
+                        const uint64_t bd = sdesc_kmajor_sw128(b0 + ks * MMA_KB);
+                        const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
+                        if constexpr (KIND == Kind::I8)
+                            mma_i8_pair(d, ad, bd, idesc, accum);
+                        else
+                            mma_f16_pair(d, ad, bd, idesc, accum);
+                    }
+                    mma_commit_pair(empty_own + 8u * stage);
+                    mma_commit_pair(empty_peer + 8u * stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                mma_commit_pair(tfull_own + 8u * acc);
+                mma_commit_pair(tfull_peer + 8u * acc);
+            }
+            mma_commit_pair(drain_own);
+            int dummy = 0;
+            mbar_wait(drain, 0, &dummy, p.status, GK_DEV_TIMEOUT_DRAIN, tmo);
+        }
+    } else {
+        // ---------------- epilogue (warps 2 .. 9, both CTAs) ----------------
+        const int q = warp & 3;
+        const int col_base = ((warp - 2) >> 2) * C::WCOLS;
+        const int et = threadIdx.x - 64;
+        const EpiParams& e = p.e;
+        const int row = q * 32 + lane;
+        const bool col_params = C::QUANT && (e.scale_axis == AX_N || e.bias_axis == AX_N);
+
+        struct Raw {
+            float rscale, cscale;
+            int32_t rbias, cbias;
+        };
+        auto load_raw = [&](int t, Raw& r) {
+            int b, tm, tn;
+            decode_tile(t, p, b, tm, tn);
+            const int64_t grow = static_cast<int64_t>(tm) * 2 * BM + rank * BM + row;
+            const int64_t gc = static_cast<int64_t>(tn) * BN + et;
+            const bool rok = grow < p.Mk, cok = et < BN && gc < p.Nk;
+            r.rscale = e.scale;
+            r.cscale = 1.0f;
+            r.rbias = 0;
+            r.cbias = 0;
+            if (e.scale_axis == AX_M && rok) r.rscale = e.scales[b * e.scale_bs + grow];
+            if (e.bias_axis == AX_M && rok) r.rbias = e.bias[b * e.bias_bs + grow];
+            if (e.scale_axis == AX_N && cok) r.cscale = e.scales[b * e.scale_bs + gc];
+            if (e.bias_axis == AX_N && cok) r.cbias = e.bias[b * e.bias_bs + gc];
+        };
+        double r_se = 0.0, r_nms = 0.0;
+        uint32_t r_ulo = 0, r_uhi = 0, r_bp = 0x80000000u;
+        auto commit = [&](const Raw& r, int buf) {
+            if (e.scale_axis != AX_N) make_scale_param(r.rscale, r_se, r_nms, r_ulo, r_uhi);
+            r_bp = static_cast<uint32_t>(r.rbias) + 0x80000000u;
+            if (col_params) {
+                if (et < BN) {
+                    ColParam c;
+                    if (e.scale_axis == AX_N) {
+                        make_scale_param(r.cscale, c.se, c.nms, c.ulo, c.uhi);
+                    } else {
+                        c.se = 0.0;
+                        c.nms = 0.0;
+                        c.ulo = 0;
+                        c.uhi = 0;
+                    }
+                    c.bias_plus = static_cast<uint32_t>(r.cbias) + 0x80000000u;
+                    c.pad = 0;
+                    cparams[buf * BN + et] = c;
+                }
+                mbar_arrive(&pready[buf]);
+            }
+        };
+
+        Raw raw;
+        if (C::QUANT && pair < p.num_tiles) {
+            load_raw(pair, raw);
+            commit(raw, 0);
+        }
+        int local = 0;
+        for (int t = pair; t < p.num_tiles; t += npairs, ++local) {
+            int b, tm, tn;
+            decode_tile(t, p, b, tm, tn);
+            const int acc = local & 1;
+            const uint32_t aph = (local >> 1) & 1;
+            const int64_t grow = static_cast<int64_t>(tm) * 2 * BM + rank * BM + row;
+            const int64_t gcol0 = static_cast<int64_t>(tn) * BN;
+            const bool row_ok = grow < p.Mk;
+            const ColParam* cp = cparams + acc * BN;
+
+            if (col_params && !warp_wait(&pready[acc], aph, abort_flag, p.status,
+                                         GK_DEV_TIMEOUT_EPILOGUE, tmo))
+                break;
+            if (!warp_wait(&tfull[acc], aph, abort_flag, p.status, GK_DEV_TIMEOUT_EPILOGUE, tmo))
+                break;
+            tc_fence_after();
+
+            const int t_next = t + npairs;
+            Raw raw_next;
+            if (C::QUANT && t_next < p.num_tiles) load_raw(t_next, raw_next);
+
+            const int64_t obase = static_cast<int64_t>(b) * e.obs + grow * e.ldo;
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN + col_base);
+            uint32_t va[32], vb[32];
+            tmem_ld_chunk<CH>(tbase, va);
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                uint32_t(&cur)[32] = (c & 1) ? vb : va;
+                uint32_t(&nxt)[32] = (c & 1) ? va : vb;
+                tmem_wait_ld();
+                reg_fence<CH>(cur);
+                if (c + 1 < NCH) {
+                    tmem_ld_chunk<CH>(tbase + (c + 1) * CH, nxt);
+                } else {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(tempty_l + 8u * acc);
+                }
+                if (row_ok)
+                    epilogue_chunk<OUT, CH>(cur, p, e, obase, gcol0 + col_base + c * CH,
+                                            cp + col_base + c * CH, r_se, r_nms, r_ulo, r_uhi,
+                                            r_bp);
+            }
+            if (C::QUANT && t_next < p.num_tiles) commit(raw_next, acc ^ 1);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    }
+}
+
+template <Kind KIND, Out OUT, int BN>
+static int launch_pair_one(const TcProblem& pr, const TcPlan& plan, GemmParams gp, char* err,
+                           size_t errlen) {
+    using C = PairCfg<OUT, BN>;
+    constexpr int ES = (KIND == Kind::I8) ? 1 : 2;
+    CUtensorMap ta, tb;
+    int rc;
+    if (pr.a.slab)
+        rc = encode_tiled_operand(&ta, pr.a, pr.K, BM, err, errlen);
+    else
+        rc = encode_operand(&ta, pr.a, pr.K, pr.batch, ES, BM, err, errlen);
+    if (rc) return rc;
+    if (pr.b.slab)
+        rc = encode_tiled_operand(&tb, pr.b, pr.K, BN / 2, err, errlen);
+    else
+        rc = encode_operand(&tb, pr.b, pr.K, pr.batch, ES, BN / 2, err, errlen);
+    if (rc) return rc;
+    gp.a_tiled = pr.a.slab ? static_cast<const uint8_t*>(pr.a.ptr) : nullptr;
+    gp.b_tiled = pr.b.slab ? static_cast<const uint8_t*>(pr.b.ptr) : nullptr;
+    gp.a_slab = pr.a.slab;
+    gp.b_slab = pr.b.slab;
+    auto kern = tc_gemm_pair_kernel<KIND, OUT, BN>;
+    static int attr_done[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_done[dev & 63]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) {
+            snprintf(err, errlen, "gemmkit: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+            return 3;
+        }
+        attr_done[dev & 63] = 1;
+    }
+    gp.tiles_n = plan.tiles_n;
+    gp.tiles_per_batch = gp.tiles_m * gp.tiles_n;
+    gp.num_tiles = plan.num_tiles;
+    gp.dp_tiles = plan.num_tiles;
+
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    // A persistent grid must be co-resident: GPC boundaries can leave fewer two-SM clusters
+    // than SMs / 2, so ask the runtime how many clusters of this kernel fit at once.
+    static int max_clusters[64] = {0};
+    int grid = plan.grid;
+    {
+        cudaLaunchConfig_t q;
+        memset(&q, 0, sizeof(q));
+        q.gridDim = dim3(static_cast<unsigned>(plan.grid));
+        q.blockDim = dim3(C::THREADS);
+        q.dynamicSmemBytes = C::SMEM;
+        cudaLaunchAttribute qa[1];
+        qa[0].id = cudaLaunchAttributeClusterDimension;
+        qa[0].val.clusterDim.x = 2;
+        qa[0].val.clusterDim.y = 1;
+        qa[0].val.clusterDim.z = 1;
+        q.attrs = qa;
+        q.numAttrs = 1;
+        if (!max_clusters[dev & 63]) {
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess || n <= 0) {
+                cudaGetLastError();
+                n = 1;
+            }
+            max_clusters[dev & 63] = n;
+        }
+        const int tiles = plan.num_tiles;
+        const int pairs = tiles < max_clusters[dev & 63] ? tiles : max_clusters[dev & 63];
+        grid = 2 * pairs;
+    }
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = pr.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, gp);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        snprintf(err, errlen, "gemmkit: pair kernel launch failed: %s", cudaGetErrorString(e));
+        return 3;
+    }
+    return 0;
+}
+
+int launch_pair(const TcProblem& pr, const TcPlan& plan, const GemmParams& gp, char* err,
+                size_t errlen) {
+#define GK_PAIR_CASE(K, O)                                                               \
+    if (pr.kind == K && pr.out == O)                                                     \
+        return plan.bn == 256 ? launch_pair_one<K, O, 256>(pr, plan, gp, err, errlen)    \
+                              : launch_pair_one<K, O, 128>(pr, plan, gp, err, errlen);
+    GK_PAIR_CASE(Kind::I8, Out::I32)
+    GK_PAIR_CASE(Kind::I8, Out::Q8)
+    GK_PAIR_CASE(Kind::I8, Out::U8)
+    GK_PAIR_CASE(Kind::BF16, Out::F32)
+    GK_PAIR_CASE(Kind::F16, Out::F32)
+#undef GK_PAIR_CASE
+    snprintf(err, errlen, "gemmkit: internal error: unsupported pair kernel combination");
+    return 1;
+}
+
+}  // namespace gk

@@ -138,3 +138,18 @@ def test_half_stream_k_beta(shape):
     assert np.array_equal(outs[0], outs[1])  # deterministic reduction order
     rows = np.arange(0, m, 37)
     check(outs[0], a, b, 1.5, 0.5, c0, False, rows=rows)
+
+
+@pytest.mark.parametrize("is_f16", [False, True])
+def test_half_pair_odd_shape(is_f16):
+    m, k, n = 2341, 300, 2315
+    rng = np.random.default_rng(31 + is_f16)
+    a = make(rng, (m, k), is_f16)
+    b = make(rng, (k, n), is_f16)
+    c0 = rng.standard_normal((m, n)).astype(np.float32)
+    da, db = dev(a.view(np.int16)), dev(np.ascontiguousarray(b.T).view(np.int16))
+    dc = dev(c0)
+    gk.gemm_half_f32(1.0, gk.MatRef.from_row_major(da, m, k), gk.MatRef.new(db, k, n, 1, k), -0.5,
+                     gk.MatMut.from_row_major(dc, m, n), is_f16=is_f16)
+    rows = np.concatenate([np.arange(0, m, 97), [m - 1]])
+    check(host(dc).reshape(m, n), a, b, 1.0, -0.5, c0, is_f16, rows=rows)

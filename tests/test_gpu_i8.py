@@ -466,3 +466,64 @@ def test_stream_k_prepacked_gemv_sizes():
         gk.gemm_i8_packed_b_requant(M, ptr(da), k, 1, packed, gk.Requantize(
             gk.RequantScale.PerCol(dsc), 3), ptr(dc), n, 1)
         assert np.array_equal(host(dc).reshape(M, n), want), (M, k, n)
+
+
+# ---- CTA-pair kernel (256 x 256 tiles over two SMs) ------------------------------------------
+
+PAIR_SHAPE = (2341, 300, 2315)  # >= 74 pair tiles, odd edges in every dimension, K % 128 != 0
+
+
+def test_pair_i32_odd_shape():
+    m, k, n = PAIR_SHAPE
+    rng = np.random.default_rng(21)
+    a = rand_i8(rng, (m, k))
+    bT = rand_i8(rng, (n, k))
+    c0 = rng.integers(-1000, 1000, (m, n)).astype(np.int32)
+    rows = np.sort(rng.choice(m, 48, replace=False))
+    want = O.gemm_i8_matrix(-3, a[rows], bT.T, 2, c0[rows])
+    da, db, dc = dev(a), dev(bT), dev(c0)
+    gk.gemm_i8(-3, gk.MatRef.from_row_major(da, m, k), gk.MatRef.new(db, k, n, 1, k), 2,
+               gk.MatMut.from_row_major(dc, m, n))
+    got = host(dc).reshape(m, n)
+    assert np.array_equal(got[rows], want)
+    assert np.array_equal(got[-1], O.gemm_i8_matrix(-3, a[-1:], bT.T, 2, c0[-1:])[0])
+
+
+@pytest.mark.parametrize("out_u8", [False, True])
+def test_pair_requant_odd_shape(out_u8):
+    m, k, n = PAIR_SHAPE
+    rng = np.random.default_rng(22 + out_u8)
+    a = rand_i8(rng, (m, k), -127, 127)
+    bT = rand_i8(rng, (n, k), -127, 127)
+    bias = rng.integers(-2**15, 2**15 + 1, m).astype(np.int32)
+    scales = rng.uniform(1e-4, 1e-3, n).astype(np.float32)
+    zp = 9 if out_u8 else -4
+    rows = np.sort(np.concatenate([rng.choice(m, 40, replace=False), [m - 1]]))
+    want = O.requant_matrix(a[rows], bT.T, scales=scales, scale_axis="col", bias=bias[rows],
+                            bias_axis="row", zp=zp, out_u8=out_u8, relu=True)
+    da, db, dbias, dsc = dev(a), dev(bT), dev(bias), dev(scales)
+    req = gk.Requantize(gk.RequantScale.PerCol(dsc), zp, dbias, gk.AXIS_ROW, True)
+    for c_row in (True, False):
+        dc = empty(m * n, np.uint8 if out_u8 else np.int8)
+        rsc, csc = (n, 1) if c_row else (1, m)
+        gk.gemm_i8_requant_ex_unchecked(m, k, n, ptr(da), k, 1, ptr(db), 1, k, req, ptr(dc), rsc,
+                                        csc, out_u8=out_u8)
+        got = gather(host(dc), m, n, rsc, csc)
+        assert np.array_equal(got[rows], want), c_row
+
+
+def test_pair_prepacked_batched_c4_shape():
+    """Batched config 4 elements go to the pair kernel (2 x 2 pair tiles each)."""
+    rng = np.random.default_rng(23)
+    batch, m, n, k = 40, 512, 512, 128
+    a, bT, bias, scales = _c4_inputs(rng, batch, m, n, k)
+    da, dbT, dbias, dsc = dev(a), dev(bT), dev(bias), dev(scales)
+    req = gk.Requantize(gk.RequantScale.PerCol(dsc), 128, dbias, gk.AXIS_ROW)
+    dc = empty(batch * m * n, np.uint8)
+    gk.gemm_i8_requant_batched(batch, m, k, n, ptr(da), k, 1, m * k, ptr(dbT), 1, k, n * k, req,
+                               m, n, ptr(dc), 1, m, m * n, out_u8=True)
+    got = host(dc).reshape(batch, n, m)
+    for e in (0, 17, batch - 1):
+        want = O.requant_matrix(a[e], bT[e].T, scales=scales[e], scale_axis="col",
+                                bias=bias[e], bias_axis="row", zp=128, out_u8=True)
+        assert np.array_equal(got[e].T, want), e
