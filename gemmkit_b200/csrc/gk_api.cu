@@ -95,6 +95,28 @@ bool pair_enabled() {
     return env == 1;
 }
 
+// GEMMKIT_CUDA_GEMV=0 sends small-M shapes (Nk <= 64) to the general tile kernel instead of
+// the streaming small-M kernel.
+bool gemv_enabled() {
+    static int env = -1;
+    if (env == -1) {
+        const char* s = getenv("GEMMKIT_CUDA_GEMV");
+        env = (s && s[0] == '0') ? 0 : 1;
+    }
+    return env == 1;
+}
+
+// GEMMKIT_CUDA_PDL=0 launches every kernel with plain stream ordering (no programmatic
+// dependent launch overlap with the previous kernel of the stream).
+bool pdl_enabled() {
+    static int env = -1;
+    if (env == -1) {
+        const char* s = getenv("GEMMKIT_CUDA_PDL");
+        env = (s && s[0] == '0') ? 0 : 1;
+    }
+    return env == 1;
+}
+
 int tile_n_override() {
     if (g_tile_n >= 0) return g_tile_n;
     static int env = -2;
@@ -466,8 +488,13 @@ int execute(const Job& j) {
     pr.e = e;
     pr.bn = tile_n_override();
     pr.stream = j.stream;
+    pr.pdl = pdl_enabled() ? 1 : 0;
+    // the planners look at which operand is in the tiled prepacked layout; the operands
+    // themselves are filled in below, once any packing has its scratch
+    pr.a.slab = ka.slab;
+    pr.b.slab = kb.slab;
     gk::TcPlan plan;
-    gk::plan_tc_gemm2(pr, streamk_enabled(), pair_enabled(), &plan);
+    gk::plan_tc_gemm2(pr, streamk_enabled(), pair_enabled(), gemv_enabled(), &plan);
     const int64_t part_bytes = round_up(plan.part_words * 4, 256);
 
     gk_workspace* ws = j.ws ? j.ws : default_ws(dev);
@@ -805,6 +832,15 @@ int gk_prepack_rhs_i8_unchecked(const int8_t* b, ptrdiff_t rsb, ptrdiff_t csb, s
             cudaFree(p->buf);
             delete p;
             return set_err(GK_ECUDA, "gemmkit: pack kernel launch failed");
+        }
+        // The handle is immutable from here on, like gemmkit's packed buffer: the pack is
+        // complete before it is returned, so kernels may read it ahead of their stream order.
+        e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(p->buf);
+            delete p;
+            return cuda_err(e, "prepack");
         }
     }
     *out = p;

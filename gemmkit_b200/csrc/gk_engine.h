@@ -82,6 +82,7 @@ struct TcProblem {
     EpiParams e;
     int bn;  // 0 = heuristic
     cudaStream_t stream;
+    int pdl;  // 1: kernels that support it may overlap the previous kernel of the stream
     // Scratch for a stream-K tail (see GemmParams); nullptr = no stream-K.
     uint32_t* sk_part;
     uint32_t* sk_ctr;
@@ -92,6 +93,9 @@ struct TcProblem {
 // needs). plan_tc_gemm fills it; allow_sk = false plans without a stream-K tail.
 struct TcPlan {
     int pair;  // 1: CTA-pair kernel (256-row tiles over two SMs, cluster of 2)
+    int gemv;  // 1: small-M streaming kernel (Nk <= 64; bn = its MMA N)
+    int split; // small-M kernel: CTAs (one cluster) sharing each tile's K blocks, 1 = none
+    int pdl;   // launch with programmatic stream serialization
     int bn, nepi, tiles_m, tiles_n, num_tiles, num_kb, grid;
     int dp_tiles, sk_maxc;
     int64_t sk_iters;
@@ -99,8 +103,14 @@ struct TcPlan {
     int64_t ctr_words;   // 32-bit words of sk_ctr
 };
 void plan_tc_gemm(const TcProblem& p, bool allow_sk, TcPlan* plan);
-// allow_pair enables the CTA-pair kernel where it applies (GEMMKIT_CUDA_PAIR knob).
-void plan_tc_gemm2(const TcProblem& p, bool allow_sk, bool allow_pair, TcPlan* plan);
+// allow_pair enables the CTA-pair kernel where it applies (GEMMKIT_CUDA_PAIR knob);
+// allow_gemv the small-M streaming kernel (GEMMKIT_CUDA_GEMV knob).
+void plan_tc_gemm2(const TcProblem& p, bool allow_sk, bool allow_pair, bool allow_gemv,
+                   TcPlan* plan);
+// The small-M streaming kernel (gk_gemv.cu): plan_gemv fills `plan` and returns true when the
+// problem qualifies (batch 1, 1 <= Nk <= 64, no tile-width override, activations not tiled).
+bool plan_gemv(const TcProblem& p, TcPlan* plan);
+int launch_gemv(const TcProblem& pr, const TcPlan& plan, char* err, size_t errlen);
 struct GemmParams;
 int launch_pair(const TcProblem& pr, const TcPlan& plan, const GemmParams& gp, char* err,
                 size_t errlen);

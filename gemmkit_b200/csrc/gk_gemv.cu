@@ -1,0 +1,582 @@
+// gk_gemv.cu -- the bandwidth-bound small-M path: D[Mk x Nk] = W[Mk x K] * X[Nk x K]^T for
+// Nk <= 64, where W is the large operand, streamed once from HBM (for a prepacked right-hand
+// side it is the packed buffer in the output-channel frame that the host's orientation choice
+// gives it) and X holds the few activation rows, re-read from L2 by every CTA.
+//
+// gemmkit has no dedicated integer gemv route: a gemv-shaped integer product goes through its
+// small_mn dot kernels or the general driver (gemmkit/src/dispatch/int.rs:164-200), and the
+// prepacked entry always takes the general driver (gemmkit/src/dispatch/int.rs:249-256). The
+// results are the same integers on every route because i32 wrap-around sums are associative
+// (gemmkit/src/dispatch/int.rs:190-193), which is also what lets this kernel cut K and still
+// match bit for bit.
+//
+// Design. The time of one call is a fixed start (CTA set-up, then about a microsecond before
+// the first weight block lands), the streaming phase, and the tail. Streaming runs at the HBM
+// copy rate once roughly three quarters of the SMs each keep a deep ring of 16 KB copies in
+// flight, so:
+//  * with enough 128-channel tiles, each CTA streams whole tiles (persistent over the tiles,
+//    two TMEM accumulators so one tile's epilogue overlaps the next tile's copies);
+//  * with few tiles, the K blocks of each tile are cut between the `split` CTAs of a thread-
+//    block cluster, and the partial accumulators are summed on chip: the other CTAs store
+//    theirs into the leader's (by then idle) stage ring through distributed shared memory and
+//    the leader adds them in rank order and runs the epilogue. Nothing goes through global
+//    memory, so the reduction costs two cluster barriers instead of fenced global round trips
+//    behind the streaming traffic;
+//  * launched with programmatic stream serialization, a call overlaps its set-up and its first
+//    ring of prepacked-weight copies with the tail of the previous kernel of the stream (each
+//    CTA releases the next kernel once it has issued its last copy). The
+//    weights of a prepacked handle are immutable (gk_prepack_rhs_i8 returns after the packed
+//    buffer is complete), so they may be fetched before the grid dependency resolves; the
+//    activations, scales, bias and every store wait for it (griddep_wait).
+// Roles: warp 0 streams (one 1-D bulk copy per weight block from the tiled prepacked layout, or
+// a TMA tile of a plain K-contiguous operand, plus the X block); warp 1 issues tcgen05.mma
+// M=128 x N=NB; warps 2..5 drain the accumulators (one TMEM lane quarter each).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "gk_engine.h"
+#include "gk_sm100.cuh"
+#include "gk_tc_common.cuh"
+
+namespace gk {
+
+struct GemvParams {
+    int64_t Mk, Nk;
+    int32_t num_kb, tiles;
+    int32_t split;           // CTAs (one cluster) per tile; 1 = whole tiles, persistent
+    int32_t early_weights;   // fetch the first ring of weights before griddep_wait
+    const uint8_t* w_tiled;  // tiled prepacked weights, or nullptr: load through the tensor map
+    int64_t w_slab;          // bytes between consecutive K blocks of w_tiled
+    uint64_t timeout_ns;
+    unsigned int* status;
+    EpiParams e;
+};
+
+template <int NB>
+struct GemvCfg {
+    static constexpr int W_BYTES = BM * BKB;  // one 128-channel x 128-byte weight block
+    static constexpr int X_BYTES = NB * BKB;  // the NB activation rows of the same K block
+    static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int CP_BYTES = NB * static_cast<int>(sizeof(ColParam));
+    // N = 16: a 6-stage ring (110 KB) so that two CTAs fit on an SM, one of this call and one
+    // of the next, which fills its ring while this one drains. Wider N need more registers than
+    // two CTAs allow and keep one CTA with 8 stages.
+    static constexpr int MIN_BLOCKS = NB == 16 ? 2 : 1;
+    static constexpr int STAGES_WANT = NB == 16 ? 6 : 8;
+    static constexpr int STAGES_FIT = (SMEM_LIMIT - 1024 - BAR_BYTES - CP_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT < STAGES_WANT ? STAGES_FIT : STAGES_WANT;
+    static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+    static constexpr int SLOT_BYTES = BM * NB * 4;  // one CTA's partial accumulator tile
+    static constexpr int MAX_SPLIT_RING = RING_BYTES / SLOT_BYTES + 1;
+    static constexpr int TMEM_COLS = 2 * NB < 32 ? 32 : 2 * NB;
+    static constexpr int THREADS = 192;  // producer, MMA, 4 epilogue warps
+    static constexpr int SMEM = 1024 + RING_BYTES + BAR_BYTES + CP_BYTES;
+    static constexpr int CH = NB == 16 ? 16 : 32;  // TMEM columns per load
+    static constexpr int NCH = NB / CH;
+    static_assert(SMEM <= SMEM_LIMIT, "gemv stages exceed shared memory");
+    static_assert((STAGE_BYTES % 1024) == 0, "stages must keep the 1024-byte swizzle alignment");
+};
+
+// The CTA's work items, identical for every role: whole tiles blockIdx.x, + gridDim.x, ... when
+// split == 1; else K blocks [r*num_kb/split, (r+1)*num_kb/split) of tile blockIdx.x / split,
+// r = blockIdx.x % split (the CTA's rank in its cluster).
+__device__ __forceinline__ bool gemv_next(const GemvParams& p, int& it, int& tile, int& k0,
+                                          int& k1) {
+    if (p.split > 1) {
+        if (it > 0) return false;
+        tile = static_cast<int>(blockIdx.x) / p.split;
+        const int r = static_cast<int>(blockIdx.x) - tile * p.split;
+        k0 = static_cast<int>(static_cast<int64_t>(r) * p.num_kb / p.split);
+        k1 = static_cast<int>(static_cast<int64_t>(r + 1) * p.num_kb / p.split);
+    } else {
+        tile = static_cast<int>(blockIdx.x) + it * static_cast<int>(gridDim.x);
+        if (tile >= p.tiles) return false;
+        k0 = 0;
+        k1 = p.num_kb;
+    }
+    ++it;
+    return true;
+}
+
+__device__ __forceinline__ void epi_bar_sync() {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+template <Kind KIND, Out OUT, int NB>
+__global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
+    gemv_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                const GemvParams p) {
+    using C = GemvCfg<NB>;
+    constexpr int STAGES = C::STAGES;
+    constexpr int ES = (KIND == Kind::I8) ? 1 : 2;
+    constexpr int BKE = BKB / ES;
+    constexpr bool QUANT = OUT == Out::Q8 || OUT == Out::U8;
+    constexpr int CH = C::CH, NCH = C::NCH;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sW = smem;
+    uint8_t* sX = smem + STAGES * C::W_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::RING_BYTES);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + STAGES;
+    uint64_t* tfull = bars + 2 * STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tfull + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 5);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    ColParam* cp = reinterpret_cast<ColParam*>(smem + C::RING_BYTES + C::BAR_BYTES);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint64_t tmo = p.timeout_ns;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    // the epilogue's accumulator rows, kept past the loop for the cluster reduction
+    uint32_t v[NCH][32];
+    int64_t grow = 0;
+    bool have = false;
+    double r_se = 0.0, r_nms = 0.0;
+    uint32_t r_ulo = 0, r_uhi = 0, r_bp = 0x80000000u;
+    const int q = warp & 3;  // the TMEM lane quarter an epilogue warp may read
+    const int row = q * 32 + lane;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- producer ----------------
+            if (!p.w_tiled) prefetch_tmap(&tmW);
+            prefetch_tmap(&tmX);
+            auto issue_w = [&](int stage, int tile, int kb) {
+                uint8_t* dw = sW + stage * C::W_BYTES;
+                if (p.w_tiled)
+                    bulk_load(dw,
+                              p.w_tiled + static_cast<int64_t>(kb) * p.w_slab +
+                                  static_cast<int64_t>(tile) * C::W_BYTES,
+                              C::W_BYTES, &full[stage]);
+                else
+                    tma_load_3d(dw, &tmW, &full[stage], kb * BKE, tile * BM, 0);
+            };
+            // The first ring of weight blocks, ahead of the grid dependency (prepacked only).
+            int pre = 0;
+            if (p.early_weights && p.w_tiled) {
+                int it = 0, tile, k0, k1;
+                while (pre < STAGES && gemv_next(p, it, tile, k0, k1))
+                    for (int kb = k0; kb < k1 && pre < STAGES; ++kb, ++pre) {
+                        mbar_arrive_expect_tx(&full[pre], C::STAGE_BYTES);
+                        issue_w(pre, tile, kb);
+                    }
+            }
+            griddep_wait();
+            int it = 0, tile, k0, k1;
+            int stage = 0, idx = 0;
+            uint32_t phase = 0, issued = 0, last_par = 0;
+            bool ok = true;
+            while (ok && gemv_next(p, it, tile, k0, k1)) {
+                for (int kb = k0; kb < k1; ++kb, ++idx) {
+                    if (idx >= pre) {
+                        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status,
+                                       GK_DEV_TIMEOUT_PRODUCER, tmo)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                        issue_w(stage, tile, kb);
+                    }
+                    tma_load_3d(sX + stage * C::X_BYTES, &tmX, &full[stage], kb * BKE, 0, 0);
+                    issued |= 1u << stage;
+                    last_par = (last_par & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // This CTA has asked for all its data: the next kernel of the stream may start
+            // placing its CTAs, so that their first copies queue up behind this call's last
+            // ones (triggering any earlier was measured slower: the next call's copies then
+            // compete with this call's streaming instead of filling the gap after it).
+            griddep_launch_dependents();
+            // Copies land in this CTA's shared memory: wait for the last one of every stage
+            // before the CTA may exit (they have all landed already unless a wait gave up).
+            int dummy = 0;
+            for (int st = 0; st < STAGES; ++st)
+                if (issued & (1u << st))
+                    mbar_wait(&full[st], (last_par >> st) & 1u, &dummy, p.status,
+                              GK_DEV_TIMEOUT_DRAIN, tmo);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            uint32_t idesc;
+            if constexpr (KIND == Kind::I8)
+                idesc = idesc_i8(BM, NB);
+            else
+                idesc = idesc_f16(BM, NB, KIND == Kind::BF16);
+            int it = 0, tile, k0, k1;
+            int stage = 0, local = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            while (ok && gemv_next(p, it, tile, k0, k1)) {
+                const int acc = local & 1;
+                const uint32_t aph = (local >> 1) & 1u;
+                ++local;
+                if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, p.status, GK_DEV_TIMEOUT_MMA,
+                               tmo)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * NB);
+                for (int kb = k0; kb < k1; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.status, GK_DEV_TIMEOUT_MMA,
+                                   tmo)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sW + stage * C::W_BYTES);
+                    const uint32_t b0 = smem_u32(sX + stage * C::X_BYTES);
+#pragma unroll
+                    for (int ks = 0; ks < BKB / MMA_KB; ++ks) {
+                        const uint64_t ad = sdesc_kmajor_sw128(a0 + ks * MMA_KB);
+                        const uint64_t bd = sdesc_kmajor_sw128(b0 + ks * MMA_KB);
+                        const uint32_t accum = (kb != k0 || ks != 0) ? 1u : 0u;
+                        if constexpr (KIND == Kind::I8)
+                            mma_i8(d, ad, bd, idesc, accum);
+                        else
+                            mma_f16(d, ad, bd, idesc, accum);
+                    }
+                    mma_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                mma_commit(&tfull[acc]);
+            }
+            // every MMA this CTA issued has finished before TMEM is released
+            mma_commit(drain);
+            int dummy = 0;
+            mbar_wait(drain, 0, &dummy, p.status, GK_DEV_TIMEOUT_DRAIN, tmo);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int et = threadIdx.x - 64;
+        const EpiParams& e = p.e;
+        griddep_wait();  // scales, bias and the output may belong to the previous kernel
+        if (QUANT && (e.scale_axis == AX_N || e.bias_axis == AX_N)) {
+            if (et < NB) {
+                ColParam c;
+                const bool ok = et < p.Nk;
+                const float cs = (e.scale_axis == AX_N && ok) ? e.scales[et] : 1.0f;
+                make_scale_param(cs, c.se, c.nms, c.ulo, c.uhi);
+                const int32_t cb = (e.bias_axis == AX_N && ok) ? e.bias[et] : 0;
+                c.bias_plus = static_cast<uint32_t>(cb) + 0x80000000u;
+                c.pad = 0;
+                cp[et] = c;
+            }
+            epi_bar_sync();
+        }
+
+        int it = 0, tile, k0, k1;
+        int local = 0;
+        while (gemv_next(p, it, tile, k0, k1)) {
+            const int acc = local & 1;
+            const uint32_t aph = (local >> 1) & 1u;
+            ++local;
+            grow = static_cast<int64_t>(tile) * BM + row;
+            const bool row_ok = grow < p.Mk;
+            // this row's requant constants, fetched while the MMAs run
+            if constexpr (QUANT) {
+                float rs = e.scale;
+                int32_t rb = 0;
+                if (row_ok) {
+                    if (e.scale_axis == AX_M) rs = e.scales[grow];
+                    if (e.bias_axis == AX_M) rb = e.bias[grow];
+                }
+                if (e.scale_axis != AX_N) make_scale_param(rs, r_se, r_nms, r_ulo, r_uhi);
+                r_bp = static_cast<uint32_t>(rb) + 0x80000000u;
+            }
+            if (!warp_wait(&tfull[acc], aph, abort_flag, p.status, GK_DEV_TIMEOUT_EPILOGUE, tmo))
+                break;
+            tc_fence_after();
+            const uint32_t taddr =
+                tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * NB);
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                if constexpr (CH == 16)
+                    tmem_ld_x16(taddr + c * CH, v[c]);
+                else
+                    tmem_ld_x32(taddr + c * CH, v[c]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+            have = true;
+            if (p.split > 1) break;  // one item; summed across the cluster below
+            if (row_ok) {
+#pragma unroll
+                for (int c = 0; c < NCH; ++c)
+                    epilogue_chunk<OUT, CH>(v[c], p.Nk, e, grow * e.ldo, c * CH, cp + c * CH,
+                                            r_se, r_nms, r_ulo, r_uhi, r_bp);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+
+    if (p.split > 1) {
+        // Every CTA of the cluster is past its MMAs, so the leader's stage ring is idle: the
+        // others store their accumulator rows into it (slot rank - 1), then the leader sums
+        // them in rank order.
+        const uint32_t rank = cluster_ctarank();
+        cluster_sync();
+        if (warp >= 2 && rank != 0 && have) {
+            const uint32_t dst = mapa_shared(smem_u32(sW), 0) +
+                                 (rank - 1) * C::SLOT_BYTES + static_cast<uint32_t>(row * NB * 4);
+#pragma unroll
+            for (int c = 0; c < NCH; ++c)
+#pragma unroll
+                for (int g = 0; g < CH / 4; ++g)
+                    st_cluster_v4(dst + (c * CH + 4 * g) * 4, v[c][4 * g], v[c][4 * g + 1],
+                                  v[c][4 * g + 2], v[c][4 * g + 3]);
+        }
+        cluster_sync();
+        if (warp >= 2 && rank == 0 && have && grow < p.Mk) {
+            for (int j = 1; j < p.split; ++j) {
+                const uint32_t* src = reinterpret_cast<const uint32_t*>(
+                    sW + (j - 1) * C::SLOT_BYTES + row * NB * 4);
+#pragma unroll
+                for (int c = 0; c < NCH; ++c)
+#pragma unroll
+                    for (int i = 0; i < CH; ++i) {
+                        if constexpr (KIND == Kind::I8)
+                            v[c][i] += src[c * CH + i];
+                        else
+                            v[c][i] = __float_as_uint(
+                                __fadd_rn(__uint_as_float(v[c][i]), __uint_as_float(src[c * CH + i])));
+                    }
+            }
+#pragma unroll
+            for (int c = 0; c < NCH; ++c)
+                epilogue_chunk<OUT, CH>(v[c], p.Nk, p.e, grow * p.e.ldo, c * CH, cp + c * CH,
+                                        r_se, r_nms, r_ulo, r_uhi, r_bp);
+        }
+    }
+
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+// Largest cluster count that can be resident at once for `split` (cached per kernel/split).
+template <Kind KIND, Out OUT, int NB>
+static int max_clusters(int split) {
+    static int cache[64][17];
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    int& c = cache[dev & 63][split];
+    if (c == 0) {
+        using C = GemvCfg<NB>;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(split * 64), 1, 1);
+        cfg.blockDim = dim3(C::THREADS, 1, 1);
+        cfg.dynamicSmemBytes = C::SMEM;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = static_cast<unsigned>(split);
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemv_kernel<KIND, OUT, NB>, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = -1;
+        }
+        c = n > 0 ? n : -1;
+    }
+    return c;
+}
+
+template <Kind KIND, Out OUT, int NB>
+static int launch_gemv_nb(const TcProblem& pr, const TcPlan& plan, GemvParams gp, char* err,
+                          size_t errlen) {
+    using C = GemvCfg<NB>;
+    constexpr int ES = (KIND == Kind::I8) ? 1 : 2;
+    CUtensorMap tw, tx;
+    memset(&tw, 0, sizeof(tw));
+    memset(&tx, 0, sizeof(tx));
+    int rc = 0;
+    if (pr.a.slab == 0 && (rc = encode_operand(&tw, pr.a, pr.K, 1, ES, BM, err, errlen)))
+        return rc;
+    if ((rc = encode_operand(&tx, pr.b, pr.K, 1, ES, NB, err, errlen))) return rc;
+    if (pr.a.slab && (pr.a.rows % BM)) {
+        snprintf(err, errlen, "gemmkit: internal error: tiled operand rows not padded to %d", BM);
+        return 1;
+    }
+    gp.w_tiled = pr.a.slab ? static_cast<const uint8_t*>(pr.a.ptr) : nullptr;
+    gp.w_slab = pr.a.slab;
+    auto kern = gemv_kernel<KIND, OUT, NB>;
+    static int attr_done[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_done[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             C::SMEM);
+        if (e != cudaSuccess) {
+            snprintf(err, errlen, "gemmkit: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+            return e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver ? 5 : 3;
+        }
+        attr_done[dev & 63] = 1;
+    }
+    // The K split: bounded by the partial slots the leader's ring holds, and lowered until
+    // every tile's cluster can be resident at once.
+    int split = plan.split;
+    if (split > C::MAX_SPLIT_RING) split = C::MAX_SPLIT_RING;
+    while (split > 1) {
+        const int mc = max_clusters<KIND, OUT, NB>(split);
+        if (mc >= plan.tiles_m) break;
+        --split;
+    }
+    if (split < 1) split = 1;
+    gp.split = split;
+    const int grid = split > 1 ? plan.tiles_m * split
+                               : (plan.tiles_m < sm_count() ? plan.tiles_m : sm_count());
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(C::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = pr.stream;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (plan.pdl) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (split > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = static_cast<unsigned>(split);
+        at[na].val.clusterDim.y = 1;
+        at[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, gp);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        snprintf(err, errlen, "gemmkit: kernel launch failed: %s", cudaGetErrorString(e));
+        return e == cudaErrorNoDevice || e == cudaErrorNoKernelImageForDevice ||
+                       e == cudaErrorInsufficientDriver
+                   ? 5
+                   : 3;
+    }
+    return 0;
+}
+
+template <Kind KIND, Out OUT>
+static int dispatch_gemv(const TcProblem& pr, const TcPlan& plan, const GemvParams& gp,
+                         char* err, size_t errlen) {
+    switch (plan.bn) {
+        case 16: return launch_gemv_nb<KIND, OUT, 16>(pr, plan, gp, err, errlen);
+        case 32: return launch_gemv_nb<KIND, OUT, 32>(pr, plan, gp, err, errlen);
+        case 64: return launch_gemv_nb<KIND, OUT, 64>(pr, plan, gp, err, errlen);
+        default:
+            snprintf(err, errlen, "gemmkit: unsupported small-M width %d", plan.bn);
+            return 1;
+    }
+}
+
+bool plan_gemv(const TcProblem& p, TcPlan* plan) {
+    // the activation side comes through a tensor map; a tiled operand there (a prepacked
+    // right-hand side with <= 64 columns) stays with the general kernel
+    if (p.batch != 1 || p.Nk > 64 || p.Nk < 1 || p.bn != 0 || p.b.slab != 0) return false;
+    TcPlan pl;
+    memset(&pl, 0, sizeof(pl));
+    pl.gemv = 1;
+    pl.pdl = p.pdl ? 1 : 0;
+    pl.bn = p.Nk <= 16 ? 16 : (p.Nk <= 32 ? 32 : 64);
+    pl.nepi = 4;
+    pl.tiles_m = static_cast<int>((p.Mk + BM - 1) / BM);
+    pl.tiles_n = 1;
+    pl.num_tiles = pl.tiles_m;
+    const int es = p.kind == Kind::I8 ? 1 : 2;
+    pl.num_kb = static_cast<int>((p.K * es + BKB - 1) / BKB);
+    const int sms = sm_count();
+    // Whole tiles once about three quarters of the SMs have one; else cut K inside clusters
+    // of up to 8 (portable cluster size) so that tiles * split approaches the SM count.
+    int split = 1;
+    if (static_cast<int64_t>(pl.tiles_m) * 4 < static_cast<int64_t>(sms) * 3) {
+        split = sms / pl.tiles_m;
+        if (split > 8) split = 8;
+        if (split > pl.num_kb) split = pl.num_kb;
+        if (split < 1) split = 1;
+    }
+    pl.split = split;
+    pl.grid = split > 1 ? pl.tiles_m * split : (pl.tiles_m < sms ? pl.tiles_m : sms);
+    pl.dp_tiles = pl.num_tiles;
+    *plan = pl;
+    return true;
+}
+
+int launch_gemv(const TcProblem& pr, const TcPlan& plan, char* err, size_t errlen) {
+    GemvParams gp;
+    memset(&gp, 0, sizeof(gp));
+    gp.Mk = pr.Mk;
+    gp.Nk = pr.Nk;
+    gp.num_kb = plan.num_kb;
+    gp.tiles = plan.tiles_m;
+    gp.early_weights = plan.pdl;
+    gp.timeout_ns = 4000000000ull;
+    gp.status = device_status_ptr();
+    gp.e = pr.e;
+    if (pr.kind == Kind::I8) {
+        if (pr.out == Out::I32) return dispatch_gemv<Kind::I8, Out::I32>(pr, plan, gp, err, errlen);
+        if (pr.out == Out::Q8) return dispatch_gemv<Kind::I8, Out::Q8>(pr, plan, gp, err, errlen);
+        if (pr.out == Out::U8) return dispatch_gemv<Kind::I8, Out::U8>(pr, plan, gp, err, errlen);
+    } else if (pr.out == Out::F32) {
+        if (pr.kind == Kind::BF16)
+            return dispatch_gemv<Kind::BF16, Out::F32>(pr, plan, gp, err, errlen);
+        return dispatch_gemv<Kind::F16, Out::F32>(pr, plan, gp, err, errlen);
+    }
+    snprintf(err, errlen, "gemmkit: internal error: unsupported kernel combination");
+    return 1;
+}
+
+}  // namespace gk

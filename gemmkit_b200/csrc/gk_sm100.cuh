@@ -304,6 +304,27 @@ __device__ __forceinline__ void cluster_sync() {
                  ::: "memory");
 }
 
+// 16-byte store into the shared memory of a CTA of this cluster (shared::cluster address).
+__device__ __forceinline__ void st_cluster_v4(uint32_t caddr, uint32_t a, uint32_t b, uint32_t c,
+                                              uint32_t d) {
+    asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(caddr), "r"(a), "r"(b),
+                 "r"(c), "r"(d)
+                 : "memory");
+}
+
+// ---- programmatic dependent launch ---------------------------------------------------------
+// A kernel launched with programmatic stream serialization may start while the previous
+// kernel of its stream is still running. griddep_wait() returns once that kernel has finished
+// and its memory is visible (at once when there is no such dependency); every read of data a
+// previous kernel may have written, and every write, comes after it.
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Lets the next programmatically dependent kernel of the stream start launching its CTAs.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Arrive on an mbarrier given by its shared::cluster address (own CTA or the peer).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr)

@@ -144,14 +144,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     return !__any_sync(0xffffffffu, !ok);
 }
 
-// The epilogue of one chunk of CH accumulator columns held by this thread (its row `grow`),
-// starting at column gc of the output.
+// The epilogue of one chunk of CH accumulator columns held by this thread (its row), starting
+// at column gc of the output; columns at or past Nk are not written.
 template <Out OUT, int CH>
-__device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], const GemmParams& p,
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t Nk,
                                                const EpiParams& e, int64_t obase, int64_t gc,
                                                const ColParam* cp, double r_se, double r_nms,
                                                uint32_t r_ulo, uint32_t r_uhi, uint32_t r_bp) {
-    const bool full_chunk = gc + CH <= p.Nk;
+    const bool full_chunk = gc + CH <= Nk;
     if constexpr (OUT == Out::Q8 || OUT == Out::U8) {
         constexpr bool U8 = OUT == Out::U8;
         int q[CH];
@@ -188,7 +188,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], const Ge
         } else {
 #pragma unroll
             for (int i = 0; i < CH; ++i)
-                if (gc + i < p.Nk)
+                if (gc + i < Nk)
                     out[obase + (gc + i) * e.cso] = static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3)));
         }
     } else if constexpr (OUT == Out::I32) {
@@ -217,7 +217,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], const Ge
         } else {
 #pragma unroll
             for (int i = 0; i < CH; ++i) {
-                if (gc + i >= p.Nk) continue;
+                if (gc + i >= Nk) continue;
                 int32_t* cptr = out + obase + (gc + i) * e.cso;
                 uint32_t o = al * v[i];
                 if (be != 0u) o += be * static_cast<uint32_t>(*cptr);
@@ -248,7 +248,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], const Ge
         } else {
 #pragma unroll
             for (int i = 0; i < CH; ++i) {
-                if (gc + i >= p.Nk) continue;
+                if (gc + i >= Nk) continue;
                 float* cptr = out + obase + (gc + i) * e.cso;
                 float x = al * __uint_as_float(v[i]);
                 if (be != 0.0f) x = __fmaf_rn(be, *cptr, x);

@@ -336,7 +336,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                         st_global_v4(dst + 4 * g, cur[4 * g], cur[4 * g + 1], cur[4 * g + 2],
                                      cur[4 * g + 3]);
                 } else if (row_ok) {
-                    epilogue_chunk<OUT, CH>(cur, p, e, obase, gcol0 + col_base + c * CH,
+                    epilogue_chunk<OUT, CH>(cur, p.Nk, e, obase, gcol0 + col_base + c * CH,
                                             cp + col_base + c * CH, r_se, r_nms, r_ulo, r_uhi,
                                             r_bp);
                 }
@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                             }
                         }
                         if (row_ok)
-                            epilogue_chunk<OUT, CH>(sum, p, e, obase, gcol0 + col_base + c * CH,
+                            epilogue_chunk<OUT, CH>(sum, p.Nk, e, obase, gcol0 + col_base + c * CH,
                                                     cp + col_base + c * CH, r_se, r_nms, r_ulo,
                                                     r_uhi, r_bp);
                     }
@@ -672,7 +672,9 @@ void plan_tc_gemm(const TcProblem& p, bool allow_sk, TcPlan* plan) {
     }
 }
 
-void plan_tc_gemm2(const TcProblem& p, bool allow_sk, bool allow_pair, TcPlan* plan) {
+void plan_tc_gemm2(const TcProblem& p, bool allow_sk, bool allow_pair, bool allow_gemv,
+                   TcPlan* plan) {
+    if (allow_gemv && plan_gemv(p, plan)) return;
     plan_tc_gemm(p, allow_sk, plan);
     TcPlan& pl = *plan;
     if (!allow_pair || pl.bn != 256 || p.Mk < 2 * BM) return;
@@ -724,6 +726,7 @@ int launch_tc_gemm_planned(const TcProblem& pr, const TcPlan& plan, char* err, s
     gp.timeout_ns = 4000000000ull;
     gp.status = device_status_ptr();
     gp.e = pr.e;
+    if (plan.gemv) return launch_gemv(pr, plan, err, errlen);
     if (plan.pair) return launch_pair(pr, plan, gp, err, errlen);
     if (pr.kind == Kind::I8) {
         if (pr.out == Out::I32) return dispatch_bn<Kind::I8, Out::I32>(pr, plan, gp, err, errlen);

@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
                     if (lane == 0) mbar_arrive_cluster(tempty_l + 8u * acc);
                 }
                 if (row_ok)
-                    epilogue_chunk<OUT, CH>(cur, p, e, obase, gcol0 + col_base + c * CH,
+                    epilogue_chunk<OUT, CH>(cur, p.Nk, e, obase, gcol0 + col_base + c * CH,
                                             cp + col_base + c * CH, r_se, r_nms, r_ulo, r_uhi,
                                             r_bp);
             }
