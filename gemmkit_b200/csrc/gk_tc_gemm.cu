@@ -4,21 +4,26 @@
 //   kind::i8 (s8 x s8 -> s32) with an i32 (alpha/beta) or a requantizing i8/u8 epilogue,
 //   kind::f16 (bf16 or f16 -> f32) with an f32 (alpha/beta) epilogue.
 //
-// Per CTA (one per SM, 192 threads):
+// Per CTA (one per SM; 64 + 32 * NEPI threads):
 //   warp 0  TMA producer: 128-byte-swizzled K-major boxes of A (128 rows) and B (BN rows),
-//           128 bytes of K per stage, into a STAGES-deep shared-memory ring;
+//           128 bytes of K per stage, into a STAGES-deep shared-memory ring (1-D bulk copies
+//           for operands in the tiled prepacked layout);
 //   warp 1  owns the TMEM allocation and issues tcgen05.mma (M = 128, N = BN, 32 bytes of K
 //           per instruction) into one of two TMEM accumulators, committing each stage back
 //           to the producer and each finished tile to the epilogue;
-//   warps 2-5  epilogue: tcgen05.ld of their 32 TMEM lanes, the fused epilogue in
-//           registers, and direct vector stores -- while the MMA warp already accumulates the
-//           next tile into the other TMEM buffer.
+//   warps 2 .. 1 + NEPI  epilogue (4 warps, or 8 for BN >= 64 with two column halves):
+//           tcgen05.ld of their 32 TMEM lanes, the fused epilogue in registers, and direct
+//           vector stores -- while the MMA warp already accumulates the next tile into the
+//           other TMEM buffer.
 // Every wait is bounded (globaltimer); a give-up raises a CTA abort flag, records the role in
 // the device status word, drains in-flight copies and MMAs, frees TMEM and returns.
+// Launched with programmatic stream serialization: operands, parameters, outputs and scratch
+// are touched only after griddep_wait(), and each CTA releases the next kernel of the stream
+// once its producer has issued its last copy.
 //
 // The requant arithmetic reproduces gemmkit's KRequantize::apply bit for bit
 // (gemmkit/src/kernel/epilogue.rs:810-830): q = clamp(zp + rne(fl64(f64(acc + bias) *
-// f64(scale))), LO, HI). See requant_one() for the exact-arithmetic argument.
+// f64(scale))), LO, HI). See requant_q() (gk_tc_common.cuh) for the exact-arithmetic argument.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdio.h>
@@ -117,6 +122,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer ----------------
+            griddep_wait();  // operands may be written by the previous kernel of the stream
             int stage = 0;
             uint32_t phase = 0, issued = 0, last_par = 0;
             bool ok = true;
@@ -155,6 +161,8 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                     }
                 }
             }
+            // all copies issued: the next kernel of the stream may start placing its CTAs
+            griddep_launch_dependents();
             // Drain: every issued copy has landed before the CTA may exit.
             int dummy = 0;
             for (int s = 0; s < STAGES; ++s)
@@ -275,6 +283,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
             }
         };
 
+        griddep_wait();  // parameters, outputs and stream-K scratch follow the previous kernel
         Sched sch(p);
         Work w, wn;
         bool has = sch.next(p, w);
@@ -611,8 +620,19 @@ static int launch_one(const TcProblem& pr, const TcPlan& plan, GemmParams gp, ch
         gp.sk_ctr = pr.sk_ctr;
         gp.sk_epoch = pr.sk_epoch & 0xFFFFFFu;
     }
-    kern<<<plan.grid, C::THREADS, C::SMEM, pr.stream>>>(ta, tb, gp);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(plan.grid));
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = pr.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pr.pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, gp);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         snprintf(err, errlen, "gemmkit: kernel launch failed: %s", cudaGetErrorString(e));
         return e == cudaErrorNoDevice || e == cudaErrorNoKernelImageForDevice ||

@@ -14,6 +14,15 @@
 //   tempty[a]  leader's; every epilogue warp of both CTAs arrives once it has read the tile.
 // A cluster barrier after set-up and before teardown keeps either CTA from touching the
 // other's barriers before they exist or after it has exited.
+//
+// Schedule: items t = pair, pair + npairs, ... Items below dp_tiles are whole 256 x BN tiles.
+// When the last wave would leave at least half the pairs idle, its tiles are cut into two
+// 256 x BN/2 halves (MMA N = BN/2, each CTA reading the first BN/4 rows of its B stage), so
+// the tail costs half a tile instead of a whole one.
+//
+// Programmatic dependent launch: operands, parameters and outputs are touched only after
+// griddep_wait(); each CTA releases the next kernel of the stream once its producer has issued
+// its last copy, so that kernel's CTAs launch and set up while this one drains.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdio.h>
@@ -46,6 +55,22 @@ struct PairCfg {
     static_assert(STAGES >= 2 && SMEM <= SMEM_LIMIT, "shared memory budget");
     static_assert(2 * STAGES + 7 <= BAR_BYTES / 8 - 1, "barrier area");
 };
+
+// Item t of the pair schedule: its tile, its first column inside the tile and its width.
+template <int BN>
+__device__ __forceinline__ void pair_item(int t, const GemmParams& p, int& tile, int& c0,
+                                          int& width) {
+    if (t < p.dp_tiles) {
+        tile = t;
+        c0 = 0;
+        width = BN;
+    } else {
+        const int j = t - p.dp_tiles;
+        tile = p.dp_tiles + (j >> 1);
+        c0 = (j & 1) * (BN / 2);
+        width = BN / 2;
+    }
+}
 
 template <Kind KIND, Out OUT, int BN>
 __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
@@ -82,6 +107,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
     const int pair = static_cast<int>(blockIdx.x >> 1);
     const int npairs = static_cast<int>(gridDim.x >> 1);
     const uint64_t tmo = p.timeout_ns;
+    const int n_items = p.dp_tiles + 2 * (p.num_tiles - p.dp_tiles);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -123,15 +149,20 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer (both CTAs) ----------------
+            griddep_wait();
             int stage = 0;
             uint32_t phase = 0, issued = 0, last_par = 0;
             bool ok = true;
-            for (int t = pair; t < p.num_tiles && ok; t += npairs) {
+            for (int t = pair; t < n_items && ok; t += npairs) {
+                int tile, c0, width;
+                pair_item<BN>(t, p, tile, c0, width);
                 int b, tm, tn;
-                decode_tile(t, p, b, tm, tn);
+                decode_tile(tile, p, b, tm, tn);
                 const int za = p.a_batched ? b : 0, zb = p.b_batched ? b : 0;
                 const int arow = tm * 2 * BM + static_cast<int>(rank) * BM;
-                const int brow = tn * BN + static_cast<int>(rank) * (BN / 2);
+                // this CTA's width/2 rows of B; a half item loads the full box and uses its
+                // first BN/4 rows
+                const int brow = tn * BN + c0 + static_cast<int>(rank) * (width / 2);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status,
                                    GK_DEV_TIMEOUT_PRODUCER, tmo)) {
@@ -160,6 +191,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
                     }
                 }
             }
+            griddep_launch_dependents();
             // Drain (leader): its full barriers count both CTAs' copies.
             if (leader) {
                 int dummy = 0;
@@ -172,16 +204,20 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0 && leader) {
             // ---------------- MMA issuer (leader) ----------------
-            uint32_t idesc;
-            if constexpr (KIND == Kind::I8)
-                idesc = idesc_i8(2 * BM, BN);
-            else
-                idesc = idesc_f16(2 * BM, BN, KIND == Kind::BF16);
+            uint32_t idesc_w, idesc_h;  // whole tile, half tile
+            if constexpr (KIND == Kind::I8) {
+                idesc_w = idesc_i8(2 * BM, BN);
+                idesc_h = idesc_i8(2 * BM, BN / 2);
+            } else {
+                idesc_w = idesc_f16(2 * BM, BN, KIND == Kind::BF16);
+                idesc_h = idesc_f16(2 * BM, BN / 2, KIND == Kind::BF16);
+            }
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
             int local = 0;
-            for (int t = pair; t < p.num_tiles && ok; t += npairs, ++local) {
+            for (int t = pair; t < n_items && ok; t += npairs, ++local) {
+                const uint32_t idesc = t < p.dp_tiles ? idesc_w : idesc_h;
                 const int acc = local & 1;
                 const uint32_t aph = (local >> 1) & 1;
                 if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, p.status, GK_DEV_TIMEOUT_MMA,
@@ -228,7 +264,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
     } else {
         // ---------------- epilogue (warps 2 .. 9, both CTAs) ----------------
         const int q = warp & 3;
-        const int col_base = ((warp - 2) >> 2) * C::WCOLS;
+        const int cgroup = (warp - 2) >> 2;  // which half of the item's columns this warp drains
         const int et = threadIdx.x - 64;
         const EpiParams& e = p.e;
         const int row = q * 32 + lane;
@@ -239,11 +275,13 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
             int32_t rbias, cbias;
         };
         auto load_raw = [&](int t, Raw& r) {
+            int tile, c0, width;
+            pair_item<BN>(t, p, tile, c0, width);
             int b, tm, tn;
-            decode_tile(t, p, b, tm, tn);
+            decode_tile(tile, p, b, tm, tn);
             const int64_t grow = static_cast<int64_t>(tm) * 2 * BM + rank * BM + row;
-            const int64_t gc = static_cast<int64_t>(tn) * BN + et;
-            const bool rok = grow < p.Mk, cok = et < BN && gc < p.Nk;
+            const int64_t gc = static_cast<int64_t>(tn) * BN + c0 + et;
+            const bool rok = grow < p.Mk, cok = et < width && gc < p.Nk;
             r.rscale = e.scale;
             r.cscale = 1.0f;
             r.rbias = 0;
@@ -277,21 +315,27 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
             }
         };
 
+        griddep_wait();  // parameters and outputs may belong to the previous kernel
         Raw raw;
-        if (C::QUANT && pair < p.num_tiles) {
+        if (C::QUANT && pair < n_items) {
             load_raw(pair, raw);
             commit(raw, 0);
         }
         int local = 0;
-        for (int t = pair; t < p.num_tiles; t += npairs, ++local) {
+        for (int t = pair; t < n_items; t += npairs, ++local) {
+            int tile, c0, width;
+            pair_item<BN>(t, p, tile, c0, width);
             int b, tm, tn;
-            decode_tile(t, p, b, tm, tn);
+            decode_tile(tile, p, b, tm, tn);
             const int acc = local & 1;
             const uint32_t aph = (local >> 1) & 1;
             const int64_t grow = static_cast<int64_t>(tm) * 2 * BM + rank * BM + row;
-            const int64_t gcol0 = static_cast<int64_t>(tn) * BN;
+            const int64_t gcol0 = static_cast<int64_t>(tn) * BN + c0;
             const bool row_ok = grow < p.Mk;
             const ColParam* cp = cparams + acc * BN;
+            const int wcols = width / 2;  // columns per warp group
+            const int col_base = cgroup * wcols;
+            const int nch = wcols / CH;
 
             if (col_params && !warp_wait(&pready[acc], aph, abort_flag, p.status,
                                          GK_DEV_TIMEOUT_EPILOGUE, tmo))
@@ -302,7 +346,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
 
             const int t_next = t + npairs;
             Raw raw_next;
-            if (C::QUANT && t_next < p.num_tiles) load_raw(t_next, raw_next);
+            if (C::QUANT && t_next < n_items) load_raw(t_next, raw_next);
 
             const int64_t obase = static_cast<int64_t>(b) * e.obs + grow * e.ldo;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
@@ -311,11 +355,12 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
             tmem_ld_chunk<CH>(tbase, va);
 #pragma unroll
             for (int c = 0; c < NCH; ++c) {
+                if (c >= nch) break;
                 uint32_t(&cur)[32] = (c & 1) ? vb : va;
                 uint32_t(&nxt)[32] = (c & 1) ? va : vb;
                 tmem_wait_ld();
                 reg_fence<CH>(cur);
-                if (c + 1 < NCH) {
+                if (c + 1 < nch) {
                     tmem_ld_chunk<CH>(tbase + (c + 1) * CH, nxt);
                 } else {
                     tc_fence_before();
@@ -327,7 +372,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
                                             cp + col_base + c * CH, r_se, r_nms, r_ulo, r_uhi,
                                             r_bp);
             }
-            if (C::QUANT && t_next < p.num_tiles) commit(raw_next, acc ^ 1);
+            if (C::QUANT && t_next < n_items) commit(raw_next, acc ^ 1);
         }
     }
 
@@ -409,18 +454,23 @@ static int launch_pair_one(const TcProblem& pr, const TcPlan& plan, GemmParams g
         const int tiles = plan.num_tiles;
         const int pairs = tiles < max_clusters[dev & 63] ? tiles : max_clusters[dev & 63];
         grid = 2 * pairs;
+        // Tail split: a last wave that would occupy at most half the pairs runs as half tiles.
+        const int rem = tiles % pairs;
+        if (rem > 0 && 2 * rem <= pairs) gp.dp_tiles = tiles - rem;
     }
     cfg.gridDim = dim3(static_cast<unsigned>(grid));
     cfg.blockDim = dim3(C::THREADS);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = pr.stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pr.pdl ? 2 : 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, gp);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
