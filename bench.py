@@ -45,20 +45,67 @@ def load_peaks():
 
 # ---- clocks ---------------------------------------------------------------------------------
 
+# DRAM bytes of one launch of the C2 kernel (tc_gemm_pair_kernel<I8,Q8,256>), from the ncu
+# capture summarised in profiles/tc_gemm_pair_kernel_i8_requant_c2_4096.md: 33.68 MB read +
+# 0.046 MB written (A and B read once; C stays in L2 within the launch).
+C2_TRAFFIC_BYTES = 33_726_000
+
+
 class ClockSampler:
+    """SM clock, power and clock-event reasons of this process's GPU, sampled every 10 ms
+    through NVML (read-only) from start() to stop(); the device is found by its UUID so a
+    remapped CUDA_VISIBLE_DEVICES cannot point it at another GPU. Falls back to nvidia-smi
+    (100 ms) where NVML is missing."""
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, local_index: int):
+        self.local = local_index
+        self.samples: list[tuple[float, int, float]] = []  # (sm MHz, reasons mask, W)
+        self.smax = None
         self.proc = None
         self.lines: list[str] = []
+        self._stop = threading.Event()
+        self.t = None
+        self.nvml = None
+
+    def _handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.local).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid)
 
     def start(self):
         try:
+            nv, h = self._handle()
+            self.nvml = (nv, h)
+            self.smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+
+            def loop():
+                while not self._stop.is_set():
+                    try:
+                        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                        rs = get_reasons(h)
+                        pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                        self.samples.append((float(sm), int(rs), pw))
+                    except Exception:
+                        pass
+                    self._stop.wait(0.01)
+            self.t = threading.Thread(target=loop, daemon=True)
+            self.t.start()
+            return
+        except Exception:
+            self.nvml = None
+        try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", f"--id={self.local}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
@@ -71,8 +118,20 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self) -> dict:
+        if self.nvml is not None:
+            self._stop.set()
+            self.t.join(timeout=2)
+            sm = [x[0] for x in self.samples]
+            mask = 0
+            for x in self.samples:
+                mask |= x[1]
+            reasons = sorted(k for k, b in self.REASONS.items() if mask & b)
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
+                    "sm_mhz_min": min(sm) if sm else None, "reasons": reasons,
+                    "power_w_max": round(max(x[2] for x in self.samples), 1) if sm else None,
+                    "samples": len(sm), "source": "nvml, 10 ms"}
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -94,7 +153,7 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi, 100 ms"}
 
 
 # ---- distributed plumbing -------------------------------------------------------------------
@@ -407,6 +466,64 @@ def time_steps(fn, steps: int, warmup: int, ws: int):
     return max_over_ranks(e0.elapsed_time(e1), ws)
 
 
+def e2e_pipelined_ms(w, steps: int, warmup: int, ws: int) -> float:
+    """End to end through the public call: every step copies its A in from pinned host memory,
+    runs gemm_i8_packed_b_requant and copies its requantized C back to pinned host memory.
+    Steps are pipelined over three streams (host->device copies, compute, device->host
+    copies) and two buffer sets, so one step's copies overlap its neighbours' GEMMs on the
+    copy engines; events order each buffer's reuse. The timed region (CUDA events, max over
+    ranks) opens before the first copy in and closes after the last copy out. Returns ms per
+    step."""
+    import torch
+    a_host = [torch.randint(-127, 128, (w.m * w.k,), dtype=torch.int8).pin_memory()
+              for _ in range(2)]
+    c_host = [torch.empty(w.m * w.n, dtype=torch.int8).pin_memory() for _ in range(2)]
+    s_c = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    used = [False, False]
+
+    def e2e_step(i):
+        j = i % 2
+        a, _, packed, req, c = w.sets[j]
+        if used[j]:
+            s_in.wait_event(ev_comp[j])   # the GEMM two steps back has read A_j
+            s_c.wait_event(ev_out[j])     # and C_j has been copied out
+        with torch.cuda.stream(s_in):
+            a.view(-1).copy_(a_host[j], non_blocking=True)
+        ev_in[j].record(s_in)
+        s_c.wait_event(ev_in[j])
+        w.gk.gemm_i8_packed_b_requant(w.m, a.data_ptr(), w.k, 1, packed, req, c.data_ptr(), 1,
+                                      w.m, stream=s_c.cuda_stream)
+        ev_comp[j].record(s_c)
+        s_out.wait_event(ev_comp[j])
+        with torch.cuda.stream(s_out):
+            c_host[j].copy_(c, non_blocking=True)
+        ev_out[j].record(s_out)
+        used[j] = True
+
+    for i in range(warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s_c)
+    s_in.wait_event(e0)
+    s_out.wait_event(e0)
+    for i in range(steps):
+        e2e_step(warmup + i)
+    s_c.wait_stream(s_in)
+    s_c.wait_stream(s_out)
+    e1.record(s_c)
+    torch.cuda.synchronize()
+    barrier(ws)
+    return max_over_ranks(e0.elapsed_time(e1), ws) / steps
+
+
 def cpu_baseline_c2(budget_s: float = 8.0) -> dict:
     """Oracle VNNI restatement (all host threads) on a row sample of config 2."""
     import oracle as O
@@ -521,25 +638,12 @@ def main():
     barrier(ws)
     if sampler:
         sampler.start()
-        time.sleep(0.3)
     ms = time_steps(w.step, args.steps, 0, ws)
     clocks = sampler.stop() if sampler else None
     ms_step = ms / args.steps
     value = ws * w.ops / (ms_step * 1e-3) / 1e12
 
-    # end to end through the public call: pinned host A in, requantized C out, every step
-    a_host = [torch.randint(-127, 128, (w.m * w.k,), dtype=torch.int8).pin_memory()
-              for _ in range(2)]
-    c_host = torch.empty(w.m * w.n, dtype=torch.int8).pin_memory()
-
-    def e2e_step(i):
-        a, _, packed, req, c = w.sets[i % ROTATE]
-        a.view(-1).copy_(a_host[i % 2], non_blocking=True)
-        w.gk.gemm_i8_packed_b_requant(w.m, a.data_ptr(), w.k, 1, packed, req, c.data_ptr(), 1,
-                                      w.m)
-        c_host.copy_(c, non_blocking=True)
-
-    e2e_ms = time_steps(e2e_step, args.e2e_steps, 3, ws) / args.e2e_steps
+    e2e_ms = e2e_pipelined_ms(w, args.e2e_steps, 3, ws)
     e2e_value = ws * w.ops / (e2e_ms * 1e-3) / 1e12
 
     gemv = None
@@ -575,13 +679,24 @@ def main():
                        "parallelism": f"weak: {ws} independent problems, one per GPU"},
             "roofline": {"bound": "tensor", "achieved": round(kernel_tops, 2),
                          "peak": round(int8_peak, 1), "unit": "TOPS",
-                         "frac": round(kernel_tops / int8_peak, 4), "traffic": None,
+                         "frac": round(kernel_tops / int8_peak, 4),
+                         "traffic": C2_TRAFFIC_BYTES if not os.environ.get("GEMMKIT_CUDA_PAIR",
+                                                                          "1").startswith("0")
+                         else None,
+                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                           "ncu capture of this kernel on this workload "
+                                           "(profiles/tc_gemm_pair_kernel_i8_requant_c2_4096.md)",
                          "peak_source": f"2 x bf16_tflops of {peaks['source']} peaks (B200 dense "
                                         f"int8 = 2 x dense bf16)",
-                         "kernel": "tc_gemm_kernel<I8,Q8,256>", "algorithmic_ops": w.ops},
+                         "kernel": ("tc_gemm_kernel<I8,Q8,256>"
+                                    if os.environ.get("GEMMKIT_CUDA_PAIR", "1")[:1] == "0"
+                                    else "tc_gemm_pair_kernel<I8,Q8,256>"),
+                         "algorithmic_ops": w.ops},
             "e2e": {"value": round(e2e_value, 2), "unit": "TOPS",
                     "h2d_bytes_per_step": w.m * w.k, "d2h_bytes_per_step": w.m * w.n,
-                    "ms_per_step": round(e2e_ms, 4)},
+                    "ms_per_step": round(e2e_ms, 4),
+                    "how": "public call per step with its pinned-host copy in and out, steps "
+                           "pipelined over copy-in / compute / copy-out streams"},
             "gpu_launches": args.steps * launches_before,
             "clocks": clocks,
             "cpu_baseline": cpu,
