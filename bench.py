@@ -447,6 +447,104 @@ def run_config(args, ws, rank, local):
                                        "peak_source": peaks["source"]}}), flush=True)
 
 
+def run_sharded(args, ws, rank, local):
+    """BASELINE config 3 column-sharded (and config 4 batch-sharded) over the ranks: the whole
+    problem is fixed and split (strong scaling); `value` = the whole job's rate, timed on the
+    device and maxed over ranks. With one rank the problem runs unsharded on one GPU."""
+    import torch
+    torch.cuda.set_device(local)
+    peaks = load_peaks()
+    g = None
+    if ws > 1:
+        from gemmkit_b200.shard import ShardGroup
+        g = ShardGroup()
+    if args.config == "c3s":
+        replicate = bool(1 if args.replicate is None else args.replicate)
+        m = n = k = 8192
+        gen = torch.Generator(device="cuda").manual_seed(3)  # same A, B and C on every rank
+        a = torch.randn(m * k, device="cuda", generator=gen).to(torch.bfloat16)
+        bT = torch.randn(n * k, device="cuda", generator=gen).to(torch.bfloat16)
+        c0 = torch.randn(m * n, device="cuda", generator=gen)
+        n0, n1 = g.col_range(n) if g else (0, n)
+        b_block = bT[n0 * k: n1 * k].clone()  # this rank's weight columns stay resident
+        del bT
+        if g:
+            c = g.replicated_empty(m * n, torch.float32)
+            c.tensor.copy_(c0)
+            g.fence()
+        else:
+            c = None
+            cbuf = c0.clone()
+        del c0
+        import gemmkit_b200 as gk
+
+        def step(i, rep=replicate):
+            if g:
+                g.gemm_half_f32_cols(m, k, n, 1.0, a.data_ptr(), k, 1, b_block.data_ptr(), 1, k,
+                                     0.5, c, replicate=rep, route=args.route)
+            else:
+                gk.gemm_bf16_f32_unchecked(m, k, n, 1.0, a.data_ptr(), k, 1, b_block.data_ptr(),
+                                           1, k, 0.5, cbuf.data_ptr(), 1, m)
+        ms = time_steps(step, args.steps, args.warmup, ws) / args.steps
+        ms_local = ms
+        if g and replicate:
+            ms_local = time_steps(lambda i: step(i, False), args.steps, args.warmup, ws) / args.steps
+        work = 2.0 * m * n * k
+        unit, val = "TFLOP/s", work / (ms * 1e-3) / 1e12
+        extra = {"replicate": replicate, "route": args.route if (g and replicate) else None,
+                 "columns_per_rank": n1 - n0,
+                 "ms_per_step_without_replication": round(ms_local, 5),
+                 "tflops_without_replication": round(work / (ms_local * 1e-3) / 1e12, 2),
+                 "frac_of_n_gpu_bf16_peak": round(val / (ws * peaks["bf16_tflops"]), 4)}
+        if g:
+            c.close()
+        name = "c3_gemm_bf16_f32_8192_column_sharded"
+    else:
+        replicate = bool(0 if args.replicate is None else args.replicate)
+        B, m, n, k = 512, 512, 512, 128
+        gen = torch.Generator(device="cuda").manual_seed(4)
+        a = torch.randint(-128, 128, (B * m * k,), dtype=torch.int8, device="cuda", generator=gen)
+        bT = torch.randint(-128, 128, (B * n * k,), dtype=torch.int8, device="cuda", generator=gen)
+        bias = torch.randint(-2**15, 2**15 + 1, (B * m,), dtype=torch.int32, device="cuda",
+                             generator=gen)
+        scales = (torch.rand(B * n, device="cuda", generator=gen) * 9e-4 + 1e-4).float()
+        import gemmkit_b200 as gk
+        req = gk.Requantize(gk.RequantScale.PerCol(scales), 128, bias, gk.AXIS_ROW)
+        if g and replicate:
+            c = g.replicated_empty(B * m * n, torch.uint8)
+            cptr = c.ptr()
+        else:
+            c = None
+            cbuf = torch.empty(B * m * n, dtype=torch.uint8, device="cuda")
+            cptr = cbuf.data_ptr()
+
+        def step(i):
+            if g:
+                g.gemm_i8_requant_batched_shard(B, m, k, n, a.data_ptr(), k, 1, m * k,
+                                                bT.data_ptr(), 1, k, n * k, req, m, n, cptr, 1,
+                                                m, m * n, True, c=c, replicate=replicate,
+                                                route=args.route)
+            else:
+                gk.gemm_i8_requant_batched(B, m, k, n, a.data_ptr(), k, 1, m * k, bT.data_ptr(),
+                                           1, k, n * k, req, m, n, cptr, 1, m, m * n,
+                                           out_u8=True)
+        ms = time_steps(step, args.steps, args.warmup, ws) / args.steps
+        nbytes = B * (m * k + n * k + m * n + 4 * m + 4 * n)
+        unit, val = "GB/s", nbytes / (ms * 1e-3) / 1e9
+        b0, b1 = g.batch_range(B) if g else (0, B)
+        extra = {"replicate": replicate, "route": args.route if (g and replicate) else None,
+                 "batch_per_rank": b1 - b0,
+                 "frac_of_n_gpu_hbm": round(val / (ws * peaks["hbm_gbs"]), 4)}
+        if c is not None:
+            c.close()
+        name = "c4_batched_i8_requant_u8_batch_sharded"
+    if rank == 0:
+        print(json.dumps({"config": args.config, "workload": name, "value": round(val, 2),
+                          "unit": unit, "n_gpus": ws, "scaling": "strong",
+                          "ms_per_step": round(ms, 5), "steps": args.steps,
+                          "warmup": args.warmup, **extra}), flush=True)
+
+
 def time_steps(fn, steps: int, warmup: int, ws: int):
     """CUDA-event time of exactly `steps` calls (after `warmup`), max over ranks, in ms."""
     import torch
@@ -605,7 +703,12 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gemv", action="store_true", help="skip the GEMV side measurement")
     ap.add_argument("--config", default=None,
-                    help="run one BASELINE config alone: c1, c2, c3, c4, c5 (M=16), c51, c54")
+                    help="run one BASELINE config alone: c1, c2, c3, c4, c5 (M=16), c51, c54; "
+                         "c3s / c4s: the column- / batch-sharded forms over the torchrun ranks")
+    ap.add_argument("--route", default="nvlink", choices=["nvlink", "nccl"],
+                    help="c3s/c4s: replicate C through the GEMM's peer stores or NCCL")
+    ap.add_argument("--replicate", type=int, default=None,
+                    help="c3s/c4s: 1 = every rank ends with the whole C (c3s default 1, c4s 0)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -617,6 +720,12 @@ def main():
             dist.destroy_process_group()
         return
 
+    if args.config in ("c3s", "c4s"):
+        run_sharded(args, ws, rank, local)
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
     if args.config:
         run_config(args, ws, rank, local)
         if ws > 1:

@@ -34,6 +34,10 @@ class RequantC(C.Structure):
                 ("bias_len", sz)]
 
 
+class IpcHandleC(C.Structure):
+    _fields_ = [("bytes", C.c_ubyte * 64), ("offset", C.c_uint64)]
+
+
 class ProblemC(C.Structure):
     _fields_ = [("m", sz), ("k", sz), ("n", sz), ("a", vp), ("rsa", pd), ("csa", pd),
                 ("b", vp), ("rsb", pd), ("csb", pd), ("c", vp), ("rsc", pd), ("csc", pd),
@@ -86,6 +90,16 @@ SIGNATURES = {
                                                  Parallelism, vp]),
     "gk_gemm_i8_noalloc_unchecked": (i32, [sz, sz, sz, i32, vp, pd, pd, vp, pd, pd, i32, vp, pd,
                                            pd, vp]),
+    "gk_ipc_export": (i32, [vp, C.POINTER(IpcHandleC)]),
+    "gk_ipc_open": (i32, [C.POINTER(IpcHandleC), C.POINTER(vp)]),
+    "gk_ipc_close": (i32, [vp]),
+    "gk_gemm_half_f32_mirrored_unchecked": (i32, [vp, C.c_int, sz, sz, sz, f32, vp, pd, pd, vp,
+                                                  pd, pd, f32, vp, pd, pd, C.POINTER(vp),
+                                                  C.c_int, vp]),
+    "gk_gemm_i8_requant_mirrored_unchecked": (i32, [vp, sz, sz, sz, sz, vp, pd, pd, pd, vp, pd,
+                                                    pd, pd, vp, C.POINTER(RequantC), pd, pd, vp,
+                                                    pd, pd, pd, C.c_int, C.POINTER(vp), C.c_int,
+                                                    vp]),
     "gk_set_tile_n": (i32, [C.c_int]),
     "gk_selftest_wait_timeout": (i32, [C.c_uint64, vp]),
 }

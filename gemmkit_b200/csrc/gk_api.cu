@@ -356,6 +356,8 @@ struct Job {
     int32_t zp, lo, hi;
     cudaStream_t stream;
     gk_workspace* ws;
+    int nmirror;  // copies of C that receive every output element (see EpiParams::mirror)
+    void* mirror[7];
 };
 
 struct KOp {  // an operand in the canonical frame: rows x K, element (r, p) at r*rs + p*ks
@@ -410,6 +412,8 @@ int execute(const Job& j) {
     // requant_degenerate (k == 0).
     const bool alpha_zero = (j.out == gk::Out::I32 && j.alpha_i == 0) ||
                             (j.out == gk::Out::F32 && j.alpha_f == 0.0f);
+    if ((j.k == 0 || alpha_zero) && j.nmirror > 0)
+        return set_err(GK_EINVAL, "gemmkit: mirrored outputs need k > 0 and a nonzero alpha");
     if (j.k == 0 || alpha_zero) {
         if (j.out == gk::Out::I32) {
             for (int64_t b = 0; b < j.batch; ++b) {
@@ -469,6 +473,8 @@ int execute(const Job& j) {
     }
 
     e.out = j.c;
+    e.nmirror = j.nmirror;
+    for (int i = 0; i < j.nmirror; ++i) e.mirror[i] = j.mirror[i];
     e.ldo = swap ? j.csc : j.rsc;
     e.cso = swap ? j.rsc : j.csc;
     e.obs = j.cbs;
@@ -1066,6 +1072,86 @@ int gk_gemm_half_f32_batched_unchecked(gk_workspace* ws, int is_f16, size_t batc
     (void)par_ignored(par);
     return half_f32(ws, is_f16 != 0, batch, m, k, n, alpha, a, rsa, csa, a_bs, b, rsb, csb, b_bs,
                     beta, c, rsc, csc, c_bs, stream);
+}
+
+// ---- mirrored outputs (extension) ----------------------------------------------------------
+
+static int set_mirrors(Job& j, void* const* mirrors, int nmirror) {
+    if (nmirror < 0 || nmirror > 7)
+        return set_err(GK_EINVAL, "gemmkit: at most 7 mirrored outputs (got %d)", nmirror);
+    if (nmirror && !mirrors) return set_err(GK_EINVAL, "gemmkit: null mirror list");
+    for (int i = 0; i < nmirror; ++i) {
+        if (!mirrors[i]) return set_err(GK_EINVAL, "gemmkit: null mirrored output %d", i);
+        j.mirror[i] = mirrors[i];
+    }
+    j.nmirror = nmirror;
+    return GK_OK;
+}
+
+int gk_gemm_half_f32_mirrored_unchecked(gk_workspace* ws, int is_f16, size_t m, size_t k,
+                                        size_t n, float alpha, const uint16_t* a, ptrdiff_t rsa,
+                                        ptrdiff_t csa, const uint16_t* b, ptrdiff_t rsb,
+                                        ptrdiff_t csb, float beta, float* c, ptrdiff_t rsc,
+                                        ptrdiff_t csc, void* const* mirrors, int nmirror,
+                                        gk_stream_t stream) {
+    if (m && n && !c) return set_err(GK_EINVAL, "gemmkit: null C");
+    if (m && n && k && (!a || !b)) return set_err(GK_EINVAL, "gemmkit: null A or B");
+    Job j = base_job(ws, stream);
+    int rc = set_mirrors(j, mirrors, nmirror);
+    if (rc) return rc;
+    j.kind = is_f16 ? gk::Kind::F16 : gk::Kind::BF16;
+    j.out = gk::Out::F32;
+    j.m = m;
+    j.k = k;
+    j.n = n;
+    j.a = Side{a, rsa, csa, 0};
+    j.b = Side{b, rsb, csb, 0};
+    j.c = c;
+    j.rsc = rsc;
+    j.csc = csc;
+    j.alpha_f = alpha;
+    j.beta_f = beta;
+    return execute(j);
+}
+
+int gk_gemm_i8_requant_mirrored_unchecked(gk_workspace* ws, size_t batch, size_t m, size_t k,
+                                          size_t n, const int8_t* a, ptrdiff_t rsa,
+                                          ptrdiff_t csa, ptrdiff_t a_bs, const int8_t* b,
+                                          ptrdiff_t rsb, ptrdiff_t csb, ptrdiff_t b_bs,
+                                          const gk_packed_rhs* packed, const gk_requant* req,
+                                          ptrdiff_t bias_bs, ptrdiff_t scales_bs, void* c,
+                                          ptrdiff_t rsc, ptrdiff_t csc, ptrdiff_t c_bs,
+                                          int out_u8, void* const* mirrors, int nmirror,
+                                          gk_stream_t stream) {
+    if (!req) return set_err(GK_EINVAL, "gemmkit: null requant descriptor");
+    if (batch && m && n && !c) return set_err(GK_EINVAL, "gemmkit: null C");
+    if (batch && m && n && k && (!a || (!b && !packed)))
+        return set_err(GK_EINVAL, "gemmkit: null A or B");
+    if (req->scale_axis != GK_AXIS_NONE && !req->scales)
+        return set_err(GK_EINVAL, "gemmkit: null requantize scales");
+    if (packed && (batch > 1 || packed->k != k || packed->n != n))
+        return set_err(GK_EINVAL, "gemmkit: prepacked B geometry does not match (k, n) or batch > 1");
+    Job j = base_job(ws, stream);
+    int rc = set_mirrors(j, mirrors, nmirror);
+    if (rc) return rc;
+    j.kind = gk::Kind::I8;
+    j.m = m;
+    j.k = k;
+    j.n = n;
+    j.batch = batch;
+    j.a = Side{a, rsa, csa, a_bs};
+    j.b = Side{b, rsb, csb, b_bs};
+    j.packed = packed;
+    j.c = c;
+    j.rsc = rsc;
+    j.csc = csc;
+    j.cbs = c_bs;
+    fill_requant(j, req, out_u8 != 0);
+    j.bias_bs = bias_bs;
+    j.scale_bs = scales_bs;
+    if (batch > 1 && c_bs == 0 && m && n)
+        return set_err(GK_EINVAL, "gemmkit: batched C elements must not alias (c_bs == 0)");
+    return execute(j);
 }
 
 // ---- self test -----------------------------------------------------------------------------

@@ -33,6 +33,11 @@ struct EpiParams {
     int32_t zp, lo, hi;  // lo already raised to clamp(zp) under ReLU
     int32_t relu;        // apply the raised lower clamp (the band's own clamp is a saturation)
     int32_t vec;         // cso == 1 and every row start 16-byte aligned
+    // Mirrors: every output element is also stored at the same byte offset from each of
+    // mirror[0 .. nmirror) (peer GPUs' copies of C, mapped into this process), so one GEMM
+    // both computes its block and replicates it over NVLink.
+    int32_t nmirror;
+    void* mirror[7];
 };
 
 struct GemmParams {

@@ -394,6 +394,8 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
         }
     }
 
+    // mirrored outputs went to peer GPUs: make them visible system-wide before exiting
+    if (p.e.nmirror > 0 && warp >= 2) __threadfence_system();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, C::TMEM_COLS);

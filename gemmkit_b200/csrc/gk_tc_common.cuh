@@ -144,6 +144,19 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     return !__any_sync(0xffffffffu, !ok);
 }
 
+// Output stores: the local C and every mirror (same byte offset).
+__device__ __forceinline__ void out_v4(const EpiParams& e, int64_t byte_off, uint32_t a,
+                                       uint32_t b, uint32_t c, uint32_t d) {
+    st_global_v4(static_cast<uint8_t*>(e.out) + byte_off, a, b, c, d);
+    for (int i = 0; i < e.nmirror; ++i)
+        st_global_v4(static_cast<uint8_t*>(e.mirror[i]) + byte_off, a, b, c, d);
+}
+template <typename T>
+__device__ __forceinline__ void out_1(const EpiParams& e, int64_t elem_off, T v) {
+    static_cast<T*>(e.out)[elem_off] = v;
+    for (int i = 0; i < e.nmirror; ++i) static_cast<T*>(e.mirror[i])[elem_off] = v;
+}
+
 // The epilogue of one chunk of CH accumulator columns held by this thread (its row), starting
 // at column gc of the output; columns at or past Nk are not written.
 template <Out OUT, int CH>
@@ -179,17 +192,16 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t 
 #pragma unroll
         for (int g = 0; g < CH / 4; ++g)
             w[g] = pack4_sat<U8>(q[4 * g], q[4 * g + 1], q[4 * g + 2], q[4 * g + 3]);
-        uint8_t* out = static_cast<uint8_t*>(e.out);
         if (e.vec && full_chunk) {
-            uint8_t* dst = out + obase + gc;
 #pragma unroll
             for (int g = 0; g < CH / 16; ++g)
-                st_global_v4(dst + g * 16, w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+                out_v4(e, obase + gc + g * 16, w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
         } else {
 #pragma unroll
             for (int i = 0; i < CH; ++i)
                 if (gc + i < Nk)
-                    out[obase + (gc + i) * e.cso] = static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3)));
+                    out_1<uint8_t>(e, obase + (gc + i) * e.cso,
+                                   static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3))));
         }
     } else if constexpr (OUT == Out::I32) {
         int32_t* out = static_cast<int32_t*>(e.out);
@@ -213,15 +225,16 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t 
             }
 #pragma unroll
             for (int g = 0; g < CH / 4; ++g)
-                st_global_v4(dst + g * 4, r[g * 4], r[g * 4 + 1], r[g * 4 + 2], r[g * 4 + 3]);
+                out_v4(e, (obase + gc + g * 4) * 4, r[g * 4], r[g * 4 + 1], r[g * 4 + 2],
+                       r[g * 4 + 3]);
         } else {
 #pragma unroll
             for (int i = 0; i < CH; ++i) {
                 if (gc + i >= Nk) continue;
-                int32_t* cptr = out + obase + (gc + i) * e.cso;
+                const int64_t off = obase + (gc + i) * e.cso;
                 uint32_t o = al * v[i];
-                if (be != 0u) o += be * static_cast<uint32_t>(*cptr);
-                *cptr = static_cast<int32_t>(o);
+                if (be != 0u) o += be * static_cast<uint32_t>(out[off]);
+                out_1<int32_t>(e, off, static_cast<int32_t>(o));
             }
         }
     } else {  // F32
@@ -242,20 +255,90 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t 
                     x2 = __fmaf_rn(be, __uint_as_float(cv.z), x2);
                     x3 = __fmaf_rn(be, __uint_as_float(cv.w), x3);
                 }
-                st_global_v4(dst + g * 4, __float_as_uint(x0), __float_as_uint(x1),
-                             __float_as_uint(x2), __float_as_uint(x3));
+                out_v4(e, (obase + gc + g * 4) * 4, __float_as_uint(x0), __float_as_uint(x1),
+                       __float_as_uint(x2), __float_as_uint(x3));
             }
         } else {
 #pragma unroll
             for (int i = 0; i < CH; ++i) {
                 if (gc + i >= Nk) continue;
-                float* cptr = out + obase + (gc + i) * e.cso;
+                const int64_t off = obase + (gc + i) * e.cso;
                 float x = al * __uint_as_float(v[i]);
-                if (be != 0.0f) x = __fmaf_rn(be, *cptr, x);
-                *cptr = x;
+                if (be != 0.0f) x = __fmaf_rn(be, out[off], x);
+                out_1<float>(e, off, x);
             }
         }
     }
+}
+
+// A full 32-column chunk of 4-byte outputs (i32 or f32) with mirrored copies, the whole warp
+// together (the caller checks e.vec, e.nmirror > 0 and that the chunk is inside Nk, all
+// uniform across the warp; rows past Mk pass row_ok = false). The local C gets each lane's
+// 128 bytes directly. For the mirrors (peer GPUs over NVLink) the warp's 32 x 32 block goes
+// through a 4 KB shared-memory tile (16-byte pieces XOR-swizzled by row, conflict-free on both
+// sides), so that every store instruction writes four whole 128-byte lines instead of 32
+// separate 16-byte pieces.
+template <Out OUT>
+__device__ __forceinline__ void epilogue_chunk_mirrored_wide(const uint32_t (&v)[32],
+                                                             const EpiParams& e, int64_t obase,
+                                                             int64_t gc, bool row_ok,
+                                                             uint32_t* stage, int lane) {
+    static_assert(OUT == Out::I32 || OUT == Out::F32, "4-byte outputs only");
+    uint32_t r[32];
+    const int64_t off = obase + gc;  // element offset of this lane's 32 outputs
+    if constexpr (OUT == Out::I32) {
+        const uint32_t al = static_cast<uint32_t>(e.alpha_i);
+        const uint32_t be = static_cast<uint32_t>(e.beta_i);
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            uint4 cv = make_uint4(0u, 0u, 0u, 0u);
+            if (be != 0u && row_ok) cv = ld_global_v4(static_cast<int32_t*>(e.out) + off + 4 * g);
+            r[4 * g + 0] = be * cv.x + al * v[4 * g + 0];
+            r[4 * g + 1] = be * cv.y + al * v[4 * g + 1];
+            r[4 * g + 2] = be * cv.z + al * v[4 * g + 2];
+            r[4 * g + 3] = be * cv.w + al * v[4 * g + 3];
+        }
+    } else {
+        const float al = e.alpha_f, be = e.beta_f;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            float x[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) x[t] = al * __uint_as_float(v[4 * g + t]);
+            if (be != 0.0f && row_ok) {
+                const uint4 cv = ld_global_v4(static_cast<float*>(e.out) + off + 4 * g);
+                x[0] = __fmaf_rn(be, __uint_as_float(cv.x), x[0]);
+                x[1] = __fmaf_rn(be, __uint_as_float(cv.y), x[1]);
+                x[2] = __fmaf_rn(be, __uint_as_float(cv.z), x[2]);
+                x[3] = __fmaf_rn(be, __uint_as_float(cv.w), x[3]);
+            }
+#pragma unroll
+            for (int t = 0; t < 4; ++t) r[4 * g + t] = __float_as_uint(x[t]);
+        }
+    }
+    uint8_t* local = static_cast<uint8_t*>(e.out) + off * 4;
+    const int sw = lane & 7;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+        if (row_ok) st_global_v4(local + g * 16, r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
+        *reinterpret_cast<uint4*>(stage + (lane * 8 + (g ^ sw)) * 4) =
+            make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
+    }
+    __syncwarp();
+    const int piece = lane & 7;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int src = 4 * i + (lane >> 3);  // the row whose piece this lane stores
+        const long long soff = __shfl_sync(0xffffffffu, static_cast<long long>(off), src);
+        const int sok = __shfl_sync(0xffffffffu, row_ok ? 1 : 0, src);
+        const uint4 x = *reinterpret_cast<const uint4*>(stage + (src * 8 + (piece ^ (src & 7))) * 4);
+        if (sok) {
+            const int64_t boff = static_cast<int64_t>(soff) * 4 + piece * 16;
+            for (int mi = 0; mi < e.nmirror; ++mi)
+                st_global_v4(static_cast<uint8_t*>(e.mirror[mi]) + boff, x.x, x.y, x.z, x.w);
+        }
+    }
+    __syncwarp();  // the tile is reused by the next chunk
 }
 
 // Host helpers shared by the launchers (gk_tc_gemm.cu).

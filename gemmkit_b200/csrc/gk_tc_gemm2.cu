@@ -47,9 +47,13 @@ struct PairCfg {
     static constexpr bool QUANT = (OUT == Out::Q8 || OUT == Out::U8);
     static constexpr int CP_BYTES = QUANT ? 2 * BN * 32 : 0;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int RAW_STAGES = (SMEM_LIMIT - 1024 - BAR_BYTES - CP_BYTES) / STAGE_BYTES;
+    // 4-byte outputs keep a 4 KB tile per epilogue warp for mirrored (peer) stores
+    static constexpr bool WIDE = (OUT == Out::I32 || OUT == Out::F32);
+    static constexpr int EPI_STAGE_BYTES = WIDE ? NEPI * 32 * 32 * 4 : 0;
+    static constexpr int RAW_STAGES =
+        (SMEM_LIMIT - 1024 - BAR_BYTES - CP_BYTES - EPI_STAGE_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = RAW_STAGES > 10 ? 10 : RAW_STAGES;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + CP_BYTES;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + CP_BYTES + EPI_STAGE_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static_assert(BN == 128 || BN == 256, "pair tile width");
     static_assert(STAGES >= 2 && SMEM <= SMEM_LIMIT, "shared memory budget");
@@ -99,6 +103,8 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 7);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     ColParam* cparams = reinterpret_cast<ColParam*>(smem + STAGES * C::STAGE_BYTES + C::BAR_BYTES);
+    uint32_t* epi_stage = reinterpret_cast<uint32_t*>(smem + STAGES * C::STAGE_BYTES +
+                                                      C::BAR_BYTES + C::CP_BYTES);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -367,15 +373,25 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive_cluster(tempty_l + 8u * acc);
                 }
+                const int64_t gc = gcol0 + col_base + c * CH;
+                if constexpr (C::WIDE && CH == 32) {
+                    // mirrored full chunk: the whole warp stages it (conditions warp-uniform)
+                    if (e.nmirror > 0 && e.vec && gc + CH <= p.Nk) {
+                        epilogue_chunk_mirrored_wide<OUT>(cur, e, obase, gc, row_ok,
+                                                          epi_stage + (warp - 2) * 1024, lane);
+                        continue;
+                    }
+                }
                 if (row_ok)
-                    epilogue_chunk<OUT, CH>(cur, p.Nk, e, obase, gcol0 + col_base + c * CH,
-                                            cp + col_base + c * CH, r_se, r_nms, r_ulo, r_uhi,
-                                            r_bp);
+                    epilogue_chunk<OUT, CH>(cur, p.Nk, e, obase, gc, cp + col_base + c * CH, r_se,
+                                            r_nms, r_ulo, r_uhi, r_bp);
             }
             if (C::QUANT && t_next < n_items) commit(raw_next, acc ^ 1);
         }
     }
 
+    // mirrored outputs went to peer GPUs: make them visible system-wide before exiting
+    if (p.e.nmirror > 0 && warp >= 2) __threadfence_system();
     tc_fence_before();
     __syncthreads();
     cluster_sync();

@@ -267,6 +267,49 @@ int gk_gemm_i8_noalloc_unchecked(size_t m, size_t k, size_t n, int32_t alpha, co
                                  ptrdiff_t csb, int32_t beta, int32_t *c, ptrdiff_t rsc,
                                  ptrdiff_t csc, gk_stream_t stream);
 
+/* ---- sharding across the GPUs of one node (no counterpart in gemmkit) ------------------ */
+
+/* gemmkit runs in one process. For the sharded paths each GPU has its own process; a device
+ * buffer of one process is exported as a CUDA IPC handle plus the pointer's offset inside its
+ * allocation, and the other processes of the node map it (a plain peer mapping over NVLink).
+ * gk_ipc_open reference-counts mappings of one allocation; gk_ipc_close releases one. */
+typedef struct gk_ipc_handle {
+    unsigned char bytes[64];
+    uint64_t offset;
+} gk_ipc_handle;
+int gk_ipc_export(const void *dev_ptr, gk_ipc_handle *out);
+int gk_ipc_open(const gk_ipc_handle *h, void **peer_ptr);
+int gk_ipc_close(void *peer_ptr);
+
+/* Mirrored outputs: the product of gk_gemm_bf16_f32_unchecked / gk_gemm_f16_f32_unchecked
+ * (is_f16 selects), whose epilogue also stores every element of C at the same offset from
+ * each of `mirrors[0 .. nmirror)` (nmirror <= 7; usually peer GPUs' copies of C mapped with
+ * gk_ipc_open). This is the column-sharded wide GEMM with C replicated: each GPU computes
+ * its block of columns and writes it into every GPU's C in the same kernel, tile by tile,
+ * instead of a separate all-gather. beta reads only the local C. Needs k > 0 and
+ * alpha != 0 (GK_EINVAL otherwise). The mirrors are complete once the kernel has finished
+ * and the caller has synchronised with the other GPUs (for example an NCCL barrier on the
+ * same stream). */
+int gk_gemm_half_f32_mirrored_unchecked(gk_workspace *ws, int is_f16, size_t m, size_t k,
+                                        size_t n, float alpha, const uint16_t *a, ptrdiff_t rsa,
+                                        ptrdiff_t csa, const uint16_t *b, ptrdiff_t rsb,
+                                        ptrdiff_t csb, float beta, float *c, ptrdiff_t rsc,
+                                        ptrdiff_t csc, void *const *mirrors, int nmirror,
+                                        gk_stream_t stream);
+/* The same for the requantizing i8 product: gk_gemm_i8_requant_batched_unchecked's arguments
+ * (batch >= 1; bias_bs / scales_bs the per-element strides of bias and scales), optionally
+ * with a prepacked B instead of (b, rsb, csb, b_bs) (then batch must be 1), plus mirrors.
+ * The batch-sharded path uses it to replicate each GPU's slice of a batch. */
+int gk_gemm_i8_requant_mirrored_unchecked(gk_workspace *ws, size_t batch, size_t m, size_t k,
+                                          size_t n, const int8_t *a, ptrdiff_t rsa,
+                                          ptrdiff_t csa, ptrdiff_t a_bs, const int8_t *b,
+                                          ptrdiff_t rsb, ptrdiff_t csb, ptrdiff_t b_bs,
+                                          const gk_packed_rhs *packed, const gk_requant *req,
+                                          ptrdiff_t bias_bs, ptrdiff_t scales_bs, void *c,
+                                          ptrdiff_t rsc, ptrdiff_t csc, ptrdiff_t c_bs,
+                                          int out_u8, void *const *mirrors, int nmirror,
+                                          gk_stream_t stream);
+
 /* ---- self test of the bounded-wait path ----------------------------------------------- */
 
 /* Launch a kernel that waits on an mbarrier no one arrives on, with a `timeout_ns` bound,

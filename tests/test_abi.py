@@ -200,3 +200,33 @@ def test_set_tile_n_validation():
     gk.set_tile_n(0)
     with pytest.raises(gk.GemmkitError):
         gk.set_tile_n(48)
+
+
+def test_mirrored_entries_argument_errors():
+    """The mirrored-output extensions reject bad mirror lists before touching a device."""
+    import ctypes as C
+    lib = _lib.load()
+    one = (C.c_void_p * 8)(*([C.c_void_p(16)] * 8))
+    rc = lib.gk_gemm_half_f32_mirrored_unchecked(None, 0, 4, 4, 4, 1.0, C.c_void_p(16), 4, 1,
+                                                 C.c_void_p(16), 4, 1, 0.0, C.c_void_p(16), 4, 1,
+                                                 one, 8, None)
+    assert rc == _lib.GK_EINVAL and b"at most 7 mirrored outputs" in lib.gk_last_error()
+    rc = lib.gk_gemm_half_f32_mirrored_unchecked(None, 0, 4, 4, 4, 1.0, C.c_void_p(16), 4, 1,
+                                                 C.c_void_p(16), 4, 1, 0.0, C.c_void_p(16), 4, 1,
+                                                 None, 2, None)
+    assert rc == _lib.GK_EINVAL and b"null mirror list" in lib.gk_last_error()
+    nulls = (C.c_void_p * 2)(C.c_void_p(16), None)
+    rc = lib.gk_gemm_i8_requant_mirrored_unchecked(
+        None, 1, 4, 4, 4, C.c_void_p(16), 4, 1, 0, C.c_void_p(16), 4, 1, 0, None,
+        C.byref(_lib.RequantC(1.0)), 0, 0, C.c_void_p(16), 4, 1, 0, 0, nulls, 2, None)
+    assert rc == _lib.GK_EINVAL and b"null mirrored output 1" in lib.gk_last_error()
+
+
+def test_ipc_entries_argument_errors():
+    import ctypes as C
+    lib = _lib.load()
+    assert lib.gk_ipc_export(None, None) == _lib.GK_EINVAL
+    assert lib.gk_ipc_open(None, None) == _lib.GK_EINVAL
+    assert lib.gk_ipc_close(C.c_void_p(12345)) == _lib.GK_EINVAL
+    assert b"not opened by gk_ipc_open" in lib.gk_last_error()
+    assert lib.gk_ipc_close(None) == _lib.GK_OK
