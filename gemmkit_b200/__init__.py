@@ -25,7 +25,8 @@ __all__ = [
     "prepack_rhs_i8", "prepack_rhs_i8_unchecked", "gemm_i8_packed_b", "gemm_i8_packed_b_unchecked",
     "gemm_i8_packed_b_requant", "gemm_i8_requant_batched", "gemm_i8_requant_batched_ptr",
     "gemm_half_f32", "gemm_bf16_f32_unchecked", "gemm_f16_f32_unchecked",
-    "gemm_half_f32_batched", "gemm_i8_noalloc_unchecked", "set_tile_n", "device_status", "selftest_wait_timeout",
+    "gemm_half_f32_batched", "gemm_i8_noalloc_unchecked", "set_tile_n", "knob_names", "knob_get",
+    "knob_set", "device_status", "selftest_wait_timeout",
 ]
 
 
@@ -437,6 +438,23 @@ def gemm_i8_noalloc_unchecked(m, k, n, alpha, a, rsa, csa, b, rsb, csb, beta, c,
 def set_tile_n(bn: int) -> None:
     """Force the MMA tile width (16/32/64/128/256; 0 = automatic) on this thread."""
     _check(_lib.load().gk_set_tile_n(bn))
+
+
+def knob_names() -> list[str]:
+    """The engine's knobs (gemmkit's tuning knobs, gemmkit/src/tuning.rs:585-690)."""
+    return _lib.load().gk_knob_names().decode().split(",")
+
+
+def knob_get(name: str) -> int:
+    """The value in effect: the run-time override, else the environment, else the default."""
+    v = C.c_int64()
+    _check(_lib.load().gk_knob_get(name.encode(), C.byref(v)))
+    return int(v.value)
+
+
+def knob_set(name: str, value: int) -> None:
+    """Process-wide run-time override of a knob; a negative value drops the override."""
+    _check(_lib.load().gk_knob_set(name.encode(), int(value)))
 
 
 def device_status(device: int = 0, clear: bool = True) -> int:

@@ -101,6 +101,9 @@ SIGNATURES = {
                                                     pd, pd, pd, C.c_int, C.POINTER(vp), C.c_int,
                                                     vp]),
     "gk_set_tile_n": (i32, [C.c_int]),
+    "gk_knob_names": (C.c_char_p, []),
+    "gk_knob_get": (i32, [C.c_char_p, C.POINTER(C.c_int64)]),
+    "gk_knob_set": (i32, [C.c_char_p, C.c_int64]),
     "gk_selftest_wait_timeout": (i32, [C.c_uint64, vp]),
 }
 

@@ -8,6 +8,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -74,58 +75,64 @@ int check_device(int* dev_out) {
     return GK_OK;
 }
 
-// GEMMKIT_CUDA_STREAMK=1 enables the stream-K tail (off by default: its partial reductions
-// cost more than the last wave they rebalance on the shapes measured so far).
-bool streamk_enabled() {
-    static int env = -1;
-    if (env == -1) {
-        const char* s = getenv("GEMMKIT_CUDA_STREAMK");
-        env = (s && s[0] == '1') ? 1 : 0;
-    }
-    return env == 1;
+// ---- runtime knobs ---------------------------------------------------------------------
+// gemmkit's tuning module (gemmkit/src/tuning.rs:585-690): every knob has a compiled default,
+// an environment override read once, and a process-wide override set at run time
+// (gk_knob_set, the counterpart of its set_* functions). The tuner sweeps them and writes a
+// profile of `export GEMMKIT_CUDA_*=...` lines.
+//   GEMMKIT_CUDA_BN       tile width (MMA N) of the tile kernels; 0 = chosen per shape
+//   GEMMKIT_CUDA_PAIR     1 = CTA-pair (cta_group::2) kernel for 256-wide tiles
+//   GEMMKIT_CUDA_GEMV     1 = streaming small-M kernel for Nk <= 64
+//   GEMMKIT_CUDA_PDL      1 = programmatic dependent launch (overlap with the previous kernel)
+//   GEMMKIT_CUDA_STREAMK  1 = stream-K tail for the last wave of the one-CTA kernel
+enum KnobId { K_BN = 0, K_PAIR, K_GEMV, K_PDL, K_STREAMK, K_COUNT };
+const char* const kKnobEnv[K_COUNT] = {"GEMMKIT_CUDA_BN", "GEMMKIT_CUDA_PAIR", "GEMMKIT_CUDA_GEMV",
+                                       "GEMMKIT_CUDA_PDL", "GEMMKIT_CUDA_STREAMK"};
+const int64_t kKnobDefault[K_COUNT] = {0, 1, 1, 1, 0};
+std::atomic<int64_t> g_knob_set[K_COUNT];  // value + 1; 0 = no run-time override
+
+bool knob_valid(int id, int64_t v) {
+    if (id == K_BN)
+        return v == 0 || v == 16 || v == 32 || v == 64 || v == 128 || v == 192 || v == 256;
+    return v == 0 || v == 1;
 }
 
-// GEMMKIT_CUDA_PAIR=0 disables the CTA-pair (cta_group::2) kernel for large tiles.
-bool pair_enabled() {
-    static int env = -1;
-    if (env == -1) {
-        const char* s = getenv("GEMMKIT_CUDA_PAIR");
-        env = (s && s[0] == '0') ? 0 : 1;
-    }
-    return env == 1;
+int64_t knob_env(int id) {
+    static int64_t cache[K_COUNT];
+    static std::once_flag once[K_COUNT];
+    std::call_once(once[id], [id] {
+        int64_t v = kKnobDefault[id];
+        const char* s = getenv(kKnobEnv[id]);
+        if (s && *s) {
+            char* end = nullptr;
+            const long long x = strtoll(s, &end, 10);
+            if (end && *end == '\0' && knob_valid(id, x)) v = x;
+        }
+        cache[id] = v;
+    });
+    return cache[id];
 }
 
-// GEMMKIT_CUDA_GEMV=0 sends small-M shapes (Nk <= 64) to the general tile kernel instead of
-// the streaming small-M kernel.
-bool gemv_enabled() {
-    static int env = -1;
-    if (env == -1) {
-        const char* s = getenv("GEMMKIT_CUDA_GEMV");
-        env = (s && s[0] == '0') ? 0 : 1;
-    }
-    return env == 1;
+int64_t knob(int id) {
+    const int64_t s = g_knob_set[id].load(std::memory_order_relaxed);
+    return s ? s - 1 : knob_env(id);
 }
 
-// GEMMKIT_CUDA_PDL=0 launches every kernel with plain stream ordering (no programmatic
-// dependent launch overlap with the previous kernel of the stream).
-bool pdl_enabled() {
-    static int env = -1;
-    if (env == -1) {
-        const char* s = getenv("GEMMKIT_CUDA_PDL");
-        env = (s && s[0] == '0') ? 0 : 1;
-    }
-    return env == 1;
+int knob_id(const char* name) {
+    if (!name) return -1;
+    for (int i = 0; i < K_COUNT; ++i)
+        if (strcmp(name, kKnobEnv[i]) == 0) return i;
+    return -1;
 }
+
+bool streamk_enabled() { return knob(K_STREAMK) == 1; }
+bool pair_enabled() { return knob(K_PAIR) == 1; }
+bool gemv_enabled() { return knob(K_GEMV) == 1; }
+bool pdl_enabled() { return knob(K_PDL) == 1; }
 
 int tile_n_override() {
     if (g_tile_n >= 0) return g_tile_n;
-    static int env = -2;
-    if (env == -2) {
-        const char* s = getenv("GEMMKIT_CUDA_BN");
-        int v = s ? atoi(s) : 0;
-        env = (v == 16 || v == 32 || v == 64 || v == 128 || v == 192 || v == 256) ? v : 0;
-    }
-    return env;
+    return static_cast<int>(knob(K_BN));
 }
 
 // ---- gemmkit's checked-tier validation (gemmkit/src/api.rs:188-315) -----------------------
@@ -620,6 +627,33 @@ void gk_workspace_free(gk_workspace* ws) {
     if (ws->ptr) cudaFree(ws->ptr);
     if (ws->ctr) cudaFree(ws->ctr);
     delete ws;
+}
+
+const char* gk_knob_names(void) {
+    return "GEMMKIT_CUDA_BN,GEMMKIT_CUDA_PAIR,GEMMKIT_CUDA_GEMV,GEMMKIT_CUDA_PDL,"
+           "GEMMKIT_CUDA_STREAMK";
+}
+
+int gk_knob_get(const char* name, int64_t* value) {
+    const int id = knob_id(name);
+    if (id < 0) return set_err(GK_EINVAL, "gemmkit: unknown knob %s", name ? name : "(null)");
+    if (!value) return set_err(GK_EINVAL, "gemmkit: null output pointer");
+    *value = knob(id);
+    return GK_OK;
+}
+
+int gk_knob_set(const char* name, int64_t value) {
+    const int id = knob_id(name);
+    if (id < 0) return set_err(GK_EINVAL, "gemmkit: unknown knob %s", name ? name : "(null)");
+    if (value < 0) {
+        g_knob_set[id].store(0, std::memory_order_relaxed);
+        return GK_OK;
+    }
+    if (!knob_valid(id, value))
+        return set_err(GK_EINVAL, "gemmkit: %s cannot be %lld", kKnobEnv[id],
+                       static_cast<long long>(value));
+    g_knob_set[id].store(value + 1, std::memory_order_relaxed);
+    return GK_OK;
 }
 
 int gk_set_tile_n(int bn) {

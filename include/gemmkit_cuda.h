@@ -249,6 +249,17 @@ int gk_gemm_half_f32_batched_unchecked(gk_workspace *ws, int is_f16, size_t batc
  * calls on this thread; the GEMMKIT_CUDA_BN environment knob sets the process default. */
 int gk_set_tile_n(int bn);
 
+/* The engine's knobs, the counterpart of gemmkit's tuning getters / setters
+ * (gemmkit/src/tuning.rs:660-690): a compiled default, an environment override read once
+ * (`export GEMMKIT_CUDA_...=v`, the form the tuner's profile uses) and a process-wide run-time
+ * override. gk_knob_names lists them (comma-separated): GEMMKIT_CUDA_BN (0 = per shape, or 16,
+ * 32, 64, 128, 192, 256), GEMMKIT_CUDA_PAIR, GEMMKIT_CUDA_GEMV, GEMMKIT_CUDA_PDL,
+ * GEMMKIT_CUDA_STREAMK (0 / 1). gk_knob_set with a negative value drops the run-time override;
+ * an unknown name or an out-of-range value returns GK_EINVAL. */
+const char *gk_knob_names(void);
+int gk_knob_get(const char *name, int64_t *value);
+int gk_knob_set(const char *name, int64_t value);
+
 /* ---- i8 -> i32 without allocation ------------------------------------------------------ */
 
 /* No counterpart in gemmkit. The i8 -> i32 product of gk_gemm_i8_unchecked (same arguments

@@ -1,6 +1,7 @@
 """Shared helpers for the GPU parity tests (device buffers from numpy, oracle slices)."""
 from __future__ import annotations
 
+import contextlib
 import hashlib
 
 import numpy as np
@@ -45,3 +46,17 @@ def gather(buf: np.ndarray, rows: int, cols: int, rs: int, cs: int, base: int = 
 
 def rand_i8(rng, shape, lo=-128, hi=127):
     return rng.integers(lo, hi + 1, size=shape, dtype=np.int64).astype(np.int8)
+
+
+@contextlib.contextmanager
+def knobs(**values):
+    """Run a block with engine knobs overridden (e.g. knobs(GEMMKIT_CUDA_STREAMK=1)); the
+    overrides are dropped afterwards."""
+    import gemmkit_b200 as gk
+    for name, v in values.items():
+        gk.knob_set(name, v)
+    try:
+        yield
+    finally:
+        for name in values:
+            gk.knob_set(name, -1)

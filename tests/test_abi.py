@@ -230,3 +230,26 @@ def test_ipc_entries_argument_errors():
     assert lib.gk_ipc_close(C.c_void_p(12345)) == _lib.GK_EINVAL
     assert b"not opened by gk_ipc_open" in lib.gk_last_error()
     assert lib.gk_ipc_close(None) == _lib.GK_OK
+
+
+def test_knobs_get_set_and_validation():
+    import gemmkit_b200 as gk
+    names = gk.knob_names()
+    assert names == ["GEMMKIT_CUDA_BN", "GEMMKIT_CUDA_PAIR", "GEMMKIT_CUDA_GEMV",
+                     "GEMMKIT_CUDA_PDL", "GEMMKIT_CUDA_STREAMK"]
+    base = {n: gk.knob_get(n) for n in names}
+    try:
+        gk.knob_set("GEMMKIT_CUDA_BN", 128)
+        assert gk.knob_get("GEMMKIT_CUDA_BN") == 128
+        gk.knob_set("GEMMKIT_CUDA_PAIR", 0)
+        assert gk.knob_get("GEMMKIT_CUDA_PAIR") == 0
+        with pytest.raises(gk.GemmkitError, match="cannot be 100"):
+            gk.knob_set("GEMMKIT_CUDA_BN", 100)
+        with pytest.raises(gk.GemmkitError, match="cannot be 2"):
+            gk.knob_set("GEMMKIT_CUDA_PDL", 2)
+        with pytest.raises(gk.GemmkitError, match="unknown knob"):
+            gk.knob_set("GEMMKIT_CUDA_NOPE", 1)
+    finally:
+        for n in names:
+            gk.knob_set(n, -1)  # drop the overrides
+    assert {n: gk.knob_get(n) for n in names} == base

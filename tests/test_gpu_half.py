@@ -6,7 +6,7 @@ import pytest
 
 import gemmkit_b200 as gk
 import oracle as O
-from gpu_util import dev, empty, gather, host
+from gpu_util import dev, empty, gather, host, knobs
 
 pytestmark = pytest.mark.gpu
 
@@ -130,11 +130,13 @@ def test_half_stream_k_beta(shape):
     c0 = rng.standard_normal((m, n)).astype(np.float32)
     da, db = dev(a.view(np.int16)), dev(np.ascontiguousarray(b.T).view(np.int16))
     outs = []
-    for _ in range(2):
-        dc = dev(c0)
-        gk.gemm_half_f32(1.5, gk.MatRef.from_row_major(da, m, k), gk.MatRef.new(db, k, n, 1, k),
-                         0.5, gk.MatMut.from_row_major(dc, m, n))
-        outs.append(host(dc).reshape(m, n))
+    with knobs(GEMMKIT_CUDA_STREAMK=1, GEMMKIT_CUDA_PAIR=0):
+        for _ in range(2):
+            dc = dev(c0)
+            gk.gemm_half_f32(1.5, gk.MatRef.from_row_major(da, m, k),
+                             gk.MatRef.new(db, k, n, 1, k), 0.5,
+                             gk.MatMut.from_row_major(dc, m, n))
+            outs.append(host(dc).reshape(m, n))
     assert np.array_equal(outs[0], outs[1])  # deterministic reduction order
     rows = np.arange(0, m, 37)
     check(outs[0], a, b, 1.5, 0.5, c0, False, rows=rows)

@@ -8,7 +8,7 @@ import pytest
 
 import gemmkit_b200 as gk
 import oracle as O
-from gpu_util import dev, digest, empty, gather, host, rand_i8
+from gpu_util import dev, digest, empty, gather, host, knobs, rand_i8
 from refrng import Rng, bias_vec, make_i8, rand_i8 as ref_rand_i8
 
 pytestmark = pytest.mark.gpu
@@ -424,11 +424,12 @@ def test_stream_k_i32_beta(shape):
     c0 = rng.integers(-1000, 1000, (m, n)).astype(np.int32)
     want = O.gemm_i8_matrix(3, a, bT.T, -2, c0)
     da, db = dev(a), dev(bT)
-    for _ in range(3):
-        dc = dev(c0)
-        gk.gemm_i8(3, gk.MatRef.from_row_major(da, m, k), gk.MatRef.new(db, k, n, 1, k), -2,
-                   gk.MatMut.from_row_major(dc, m, n))
-        assert np.array_equal(host(dc).reshape(m, n), want)
+    with knobs(GEMMKIT_CUDA_STREAMK=1, GEMMKIT_CUDA_PAIR=0, GEMMKIT_CUDA_GEMV=0):
+        for _ in range(3):
+            dc = dev(c0)
+            gk.gemm_i8(3, gk.MatRef.from_row_major(da, m, k), gk.MatRef.new(db, k, n, 1, k), -2,
+                       gk.MatMut.from_row_major(dc, m, n))
+            assert np.array_equal(host(dc).reshape(m, n), want)
 
 
 @pytest.mark.parametrize("out_u8", [False, True])
@@ -445,15 +446,24 @@ def test_stream_k_requant(shape, out_u8):
                             zp=zp, out_u8=out_u8, relu=True)
     da, db, dbias, dsc = dev(a), dev(bT), dev(bias), dev(scales)
     req = gk.Requantize(gk.RequantScale.PerRow(dsc), zp, dbias, gk.AXIS_COL, True)
-    for _ in range(2):
-        dc = empty(m * n, np.uint8 if out_u8 else np.int8)
-        gk.gemm_i8_requant_ex_unchecked(m, k, n, ptr(da), k, 1, ptr(db), 1, k, req, ptr(dc), n, 1,
-                                        out_u8=out_u8)
-        assert np.array_equal(host(dc).reshape(m, n), want)
+    with knobs(GEMMKIT_CUDA_STREAMK=1, GEMMKIT_CUDA_PAIR=0):
+        for _ in range(2):
+            dc = empty(m * n, np.uint8 if out_u8 else np.int8)
+            gk.gemm_i8_requant_ex_unchecked(m, k, n, ptr(da), k, 1, ptr(db), 1, k, req, ptr(dc),
+                                            n, 1, out_u8=out_u8)
+            assert np.array_equal(host(dc).reshape(m, n), want)
 
 
-def test_stream_k_prepacked_gemv_sizes():
-    """Small-M over a prepacked B of several widths (112, 50 and 7 row tiles)."""
+@pytest.mark.parametrize("path", ["streaming", "tile+stream-k"])
+def test_stream_k_prepacked_gemv_sizes(path):
+    """Small-M over a prepacked B of several widths (112, 50 and 7 row tiles), on the streaming
+    small-M kernel and on the tile kernel with its stream-K tail."""
+    kv = {} if path == "streaming" else dict(GEMMKIT_CUDA_GEMV=0, GEMMKIT_CUDA_STREAMK=1)
+    with knobs(**kv):
+        _prepacked_gemv_sizes()
+
+
+def _prepacked_gemv_sizes():
     rng = np.random.default_rng(77)
     for (M, k, n) in [(4, 4096, 14336), (9, 1024, 6400), (1, 8192, 896)]:
         a = rand_i8(rng, (M, k), -127, 127)
