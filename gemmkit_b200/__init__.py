@@ -25,7 +25,7 @@ __all__ = [
     "prepack_rhs_i8", "prepack_rhs_i8_unchecked", "gemm_i8_packed_b", "gemm_i8_packed_b_unchecked",
     "gemm_i8_packed_b_requant", "gemm_i8_requant_batched", "gemm_i8_requant_batched_ptr",
     "gemm_half_f32", "gemm_bf16_f32_unchecked", "gemm_f16_f32_unchecked",
-    "gemm_half_f32_batched", "gemm_i8_noalloc_unchecked", "set_tile_n", "knob_names", "knob_get",
+    "gemm_half_f32_batched", "gemm_half_f32_fused", "Activation", "gemm_i8_noalloc_unchecked", "set_tile_n", "knob_names", "knob_get",
     "knob_set", "device_status", "selftest_wait_timeout",
 ]
 
@@ -393,6 +393,37 @@ def gemm_half_f32(alpha: float, a: MatRef, b: MatRef, beta: float, c: MatMut, is
     """bf16 / f16 inputs, f32 accumulate and output: C <- alpha*A*B + beta*C."""
     _check(_lib.load().gk_gemm_half_f32(_ws(ws), int(is_f16), alpha, a.c(), b.c(), beta, c.c(),
                                         par.c(), _stream(stream)))
+    if sync:
+        _sync(stream)
+
+
+class Activation:
+    """gemmkit::Activation (gemmkit/src/api.rs:63): ReLU or LeakyReLU(slope)."""
+
+    def __init__(self, kind: int, slope: float = 0.0):
+        self.kind, self.slope = kind, slope
+
+    @staticmethod
+    def Relu() -> "Activation":
+        return Activation(_lib.ACT_RELU)
+
+    @staticmethod
+    def LeakyRelu(slope: float) -> "Activation":
+        return Activation(_lib.ACT_LEAKY_RELU, float(slope))
+
+
+def gemm_half_f32_fused(alpha: float, a: MatRef, b: MatRef, beta: float, c: MatMut, bias=None,
+                        bias_dim: int = AXIS_ROW, act: Optional[Activation] = None, is_f16=False,
+                        par: Parallelism = SERIAL, ws=None, stream=None,
+                        sync: bool = True) -> None:
+    """gemm_fused (gemmkit/src/api/fused.rs) on bf16 / f16 inputs with f32 output:
+    C <- act(alpha*A*B + beta*C + bias), the bias per row (AXIS_ROW, length m) or per column
+    (AXIS_COL, length n)."""
+    bp, bn = _flat(bias) if bias is not None else (0, 0)
+    _check(_lib.load().gk_gemm_half_f32_fused(
+        _ws(ws), int(is_f16), alpha, a.c(), b.c(), beta, c.c(), C.c_void_p(bp or None), bn,
+        bias_dim, act.kind if act else _lib.ACT_NONE, act.slope if act else 0.0, par.c(),
+        _stream(stream)))
     if sync:
         _sync(stream)
 

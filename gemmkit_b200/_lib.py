@@ -12,6 +12,7 @@ from . import _build
 
 GK_OK, GK_EINVAL, GK_ENOMEM, GK_ECUDA, GK_ETIMEOUT, GK_ENODEV = range(6)
 AXIS_NONE, AXIS_ROW, AXIS_COL = 0, 1, 2
+ACT_NONE, ACT_RELU, ACT_LEAKY_RELU = 0, 1, 2
 
 sz, pd, vp, i32, u32, f32 = C.c_size_t, C.c_ssize_t, C.c_void_p, C.c_int32, C.c_uint32, C.c_float
 
@@ -100,6 +101,11 @@ SIGNATURES = {
                                                     pd, pd, vp, C.POINTER(RequantC), pd, pd, vp,
                                                     pd, pd, pd, C.c_int, C.POINTER(vp), C.c_int,
                                                     vp]),
+    "gk_gemm_half_f32_fused_unchecked": (i32, [vp, C.c_int, sz, sz, sz, f32, vp, pd, pd, vp, pd,
+                                               pd, f32, vp, pd, pd, vp, C.c_int, C.c_int,
+                                               C.c_int, f32, Parallelism, vp]),
+    "gk_gemm_half_f32_fused": (i32, [vp, C.c_int, f32, MatRefC, MatRefC, f32, MatMutC, vp, sz,
+                                     C.c_int, C.c_int, f32, Parallelism, vp]),
     "gk_set_tile_n": (i32, [C.c_int]),
     "gk_knob_names": (C.c_char_p, []),
     "gk_knob_get": (i32, [C.c_char_p, C.POINTER(C.c_int64)]),

@@ -365,6 +365,10 @@ struct Job {
     gk_workspace* ws;
     int nmirror;  // copies of C that receive every output element (see EpiParams::mirror)
     void* mirror[7];
+    const float* fbias;  // fused float epilogue (f32 outputs)
+    int fbias_axis;      // gk_axis (user frame)
+    int act;             // gk_act
+    float leak;
 };
 
 struct KOp {  // an operand in the canonical frame: rows x K, element (r, p) at r*rs + p*ks
@@ -431,8 +435,18 @@ int execute(const Job& j) {
             return GK_OK;
         }
         if (j.out == gk::Out::F32) {
-            rc = gk::launch_scale_c_f32(static_cast<float*>(j.c), j.m, j.n, j.rsc, j.csc, j.cbs,
-                                        j.batch, j.beta_f, j.stream);
+            if (j.act != GK_ACT_NONE || j.fbias) {
+                gk::EpiParams fe = e;
+                fe.fbias = j.fbias;
+                fe.fbias_axis = map_axis(j.fbias ? j.fbias_axis : GK_AXIS_NONE, false);
+                fe.act = j.act;
+                fe.leak = j.leak;
+                rc = gk::launch_fused_fill_f32(static_cast<float*>(j.c), j.m, j.n, j.rsc, j.csc,
+                                               j.beta_f, fe, j.stream);
+            } else {
+                rc = gk::launch_scale_c_f32(static_cast<float*>(j.c), j.m, j.n, j.rsc, j.csc,
+                                            j.cbs, j.batch, j.beta_f, j.stream);
+            }
             return rc ? set_err(GK_ECUDA, "gemmkit: fill kernel launch failed") : GK_OK;
         }
         e.bias_axis = map_axis(j.bias ? j.bias_axis : GK_AXIS_NONE, false);
@@ -480,6 +494,10 @@ int execute(const Job& j) {
     }
 
     e.out = j.c;
+    e.fbias = j.fbias;
+    e.fbias_axis = map_axis(j.fbias ? j.fbias_axis : GK_AXIS_NONE, swap);
+    e.act = j.act;
+    e.leak = j.leak;
     e.nmirror = j.nmirror;
     for (int i = 0; i < j.nmirror; ++i) e.mirror[i] = j.mirror[i];
     e.ldo = swap ? j.csc : j.rsc;
@@ -1106,6 +1124,77 @@ int gk_gemm_half_f32_batched_unchecked(gk_workspace* ws, int is_f16, size_t batc
     (void)par_ignored(par);
     return half_f32(ws, is_f16 != 0, batch, m, k, n, alpha, a, rsa, csa, a_bs, b, rsb, csb, b_bs,
                     beta, c, rsc, csc, c_bs, stream);
+}
+
+// ---- fused float epilogue (gemm_fused on the half -> f32 GEMM) -------------------------------
+
+static int half_fused(gk_workspace* ws, bool f16, size_t m, size_t k, size_t n, float alpha,
+                      const uint16_t* a, ptrdiff_t rsa, ptrdiff_t csa, const uint16_t* b,
+                      ptrdiff_t rsb, ptrdiff_t csb, float beta, float* c, ptrdiff_t rsc,
+                      ptrdiff_t csc, const float* bias, int bias_dim, int has_bias, int act,
+                      float leak, gk_stream_t stream) {
+    if (m && n && !c) return set_err(GK_EINVAL, "gemmkit: null C");
+    if (m && n && k && alpha != 0.0f && (!a || !b))
+        return set_err(GK_EINVAL, "gemmkit: null A or B");
+    if (act != GK_ACT_NONE && act != GK_ACT_RELU && act != GK_ACT_LEAKY_RELU)
+        return set_err(GK_EINVAL, "gemmkit: unknown activation %d", act);
+    if (has_bias && bias_dim != GK_AXIS_ROW && bias_dim != GK_AXIS_COL)
+        return set_err(GK_EINVAL, "gemmkit: bias dimension must be row or column");
+    if (has_bias && m && n && !bias) return set_err(GK_EINVAL, "gemmkit: null bias");
+    Job j = base_job(ws, stream);
+    j.kind = f16 ? gk::Kind::F16 : gk::Kind::BF16;
+    j.out = gk::Out::F32;
+    j.m = m;
+    j.k = k;
+    j.n = n;
+    j.a = Side{a, rsa, csa, 0};
+    j.b = Side{b, rsb, csb, 0};
+    j.c = c;
+    j.rsc = rsc;
+    j.csc = csc;
+    j.alpha_f = alpha;
+    j.beta_f = beta;
+    j.fbias = has_bias ? bias : nullptr;
+    j.fbias_axis = has_bias ? bias_dim : GK_AXIS_NONE;
+    j.act = act;
+    j.leak = act == GK_ACT_LEAKY_RELU ? leak : 0.0f;
+    return execute(j);
+}
+
+int gk_gemm_half_f32_fused_unchecked(gk_workspace* ws, int is_f16, size_t m, size_t k, size_t n,
+                                     float alpha, const uint16_t* a, ptrdiff_t rsa,
+                                     ptrdiff_t csa, const uint16_t* b, ptrdiff_t rsb,
+                                     ptrdiff_t csb, float beta, float* c, ptrdiff_t rsc,
+                                     ptrdiff_t csc, const float* bias, int bias_dim,
+                                     int has_bias, int act, float leak, gk_parallelism par,
+                                     gk_stream_t stream) {
+    (void)par_ignored(par);
+    return half_fused(ws, is_f16 != 0, m, k, n, alpha, a, rsa, csa, b, rsb, csb, beta, c, rsc,
+                      csc, bias, bias_dim, has_bias, act, leak, stream);
+}
+
+int gk_gemm_half_f32_fused(gk_workspace* ws, int is_f16, float alpha, gk_matref a, gk_matref b,
+                           float beta, gk_matmut c, const float* bias, size_t bias_len,
+                           int bias_dim, int act, float leak, gk_parallelism par,
+                           gk_stream_t stream) {
+    int rc = validate_gemm_views(a, b, c, 2, 4);
+    if (rc) return rc;
+    if (bias) {
+        // gemmkit's bias check (gemmkit/src/api.rs:318-330): the length follows its dimension
+        const size_t want = bias_dim == GK_AXIS_COL ? b.cols : a.rows;
+        if (bias_dim != GK_AXIS_ROW && bias_dim != GK_AXIS_COL)
+            return set_err(GK_EINVAL, "gemmkit: bias dimension must be row or column");
+        if (bias_len != want)
+            return set_err(GK_EINVAL, "gemmkit: %s bias length %zu does not match %s = %zu",
+                           bias_dim == GK_AXIS_COL ? "per-column" : "per-row", bias_len,
+                           bias_dim == GK_AXIS_COL ? "n" : "m", want);
+    }
+    (void)par_ignored(par);
+    return half_fused(ws, is_f16 != 0, a.rows, a.cols, b.cols, alpha,
+                      static_cast<const uint16_t*>(a.data), a.rs, a.cs,
+                      static_cast<const uint16_t*>(b.data), b.rs, b.cs, beta,
+                      static_cast<float*>(c.data), c.rs, c.cs, bias, bias_dim, bias != nullptr,
+                      act, leak, stream);
 }
 
 // ---- mirrored outputs (extension) ----------------------------------------------------------

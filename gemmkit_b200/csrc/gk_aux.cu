@@ -11,6 +11,7 @@
 
 #include "gk_engine.h"
 #include "gk_sm100.cuh"
+#include "gk_tc_common.cuh"
 
 namespace gk {
 
@@ -159,6 +160,34 @@ int launch_scale_c_f32(float* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,
     if (blocks > 4096) blocks = 4096;
     scale_c_f32_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(c, m, n, rsc, csc, cbs,
                                                                       batch, beta);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+// The fused float epilogue with a vanishing product (k == 0 or alpha == 0): C <- act(beta*C +
+// bias), gemmkit's fused degenerate rule (gemmkit/src/dispatch/float.rs:671-676); beta == 0
+// does not read C. User frame: i = row, j = column.
+__global__ void fused_fill_f32_kernel(float* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,
+                                      float beta, EpiParams e) {
+    const int64_t total = m * n;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t j = idx / m, i = idx - j * m;
+        float* p = c + i * rsc + j * csc;
+        const float x = beta == 0.0f ? 0.0f : __fmul_rn(beta, *p);
+        float bias = 0.0f;
+        if (e.fbias_axis == AX_M) bias = e.fbias[i];
+        if (e.fbias_axis == AX_N) bias = e.fbias[j];
+        *p = fused_apply(e, x, bias);
+    }
+}
+
+int launch_fused_fill_f32(float* c, int64_t m, int64_t n, int64_t rsc, int64_t csc, float beta,
+                          const EpiParams& e, cudaStream_t st) {
+    if (m == 0 || n == 0) return 0;
+    int64_t blocks = (m * n + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    fused_fill_f32_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(c, m, n, rsc, csc, beta,
+                                                                         e);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 

@@ -38,7 +38,15 @@ struct EpiParams {
     // both computes its block and replicates it over NVLink.
     int32_t nmirror;
     void* mirror[7];
+    // Fused float epilogue (f32 outputs; gemmkit's FusedEpi, gemmkit/src/kernel/epilogue.rs:
+    // 258-330): after alpha*acc + beta*C, add fbias[row or column] then apply the activation.
+    const float* fbias;
+    int32_t fbias_axis;  // Axis
+    int32_t act;         // FACT_*
+    float leak;          // LeakyReLU slope
 };
+
+enum FusedAct : int32_t { FACT_NONE = 0, FACT_RELU = 1, FACT_LEAKY = 2 };
 
 struct GemmParams {
     int64_t Mk, Nk;
@@ -144,6 +152,10 @@ int launch_scale_c_i32(int32_t* c, int64_t m, int64_t n, int64_t rsc, int64_t cs
                        cudaStream_t s);
 int launch_scale_c_f32(float* c, int64_t m, int64_t n, int64_t rsc, int64_t csc, int64_t cbs,
                        int64_t batch, float beta, cudaStream_t s);
+// Fused float epilogue with a vanishing product: C <- act(beta*C + bias) (user frame; the
+// bias axis of `e` is in the user frame too).
+int launch_fused_fill_f32(float* c, int64_t m, int64_t n, int64_t rsc, int64_t csc, float beta,
+                          const EpiParams& e, cudaStream_t s);
 // k == 0 requant fill: the map of a zero accumulator (user frame: i = row, j = col).
 int launch_requant_fill(void* c, int64_t m, int64_t n, int64_t rsc, int64_t csc, int64_t cbs,
                         int64_t batch, const EpiParams& e, cudaStream_t s);

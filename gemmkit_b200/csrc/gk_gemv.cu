@@ -166,6 +166,7 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
     bool have = false;
     double r_se = 0.0, r_nms = 0.0;
     uint32_t r_ulo = 0, r_uhi = 0, r_bp = 0x80000000u;
+    float r_fb = 0.0f;
     const int q = warp & 3;  // the TMEM lane quarter an epilogue warp may read
     const int row = q * 32 + lane;
 
@@ -316,6 +317,8 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
             grow = static_cast<int64_t>(tile) * BM + row;
             const bool row_ok = grow < p.Mk;
             // this row's requant constants, fetched while the MMAs run
+            if constexpr (OUT == Out::F32)
+                r_fb = (e.fbias_axis == AX_M && row_ok) ? e.fbias[grow] : 0.0f;
             if constexpr (QUANT) {
                 float rs = e.scale;
                 int32_t rb = 0;
@@ -347,7 +350,7 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
 #pragma unroll
                 for (int c = 0; c < NCH; ++c)
                     epilogue_chunk<OUT, CH>(v[c], p.Nk, e, grow * e.ldo, c * CH, cp + c * CH,
-                                            r_se, r_nms, r_ulo, r_uhi, r_bp);
+                                            r_se, r_nms, r_ulo, r_uhi, r_bp, r_fb);
             }
         }
     }
@@ -390,7 +393,7 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
 #pragma unroll
             for (int c = 0; c < NCH; ++c)
                 epilogue_chunk<OUT, CH>(v[c], p.Nk, p.e, grow * p.e.ldo, c * CH, cp + c * CH,
-                                        r_se, r_nms, r_ulo, r_uhi, r_bp);
+                                        r_se, r_nms, r_ulo, r_uhi, r_bp, r_fb);
         }
     }
 

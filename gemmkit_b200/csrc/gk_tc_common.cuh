@@ -144,6 +144,20 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     return !__any_sync(0xffffffffu, !ok);
 }
 
+// gemmkit's FusedEpi::apply (gemmkit/src/kernel/epilogue.rs:300-330): bias, then ReLU
+// (v > 0 ? v : 0, so NaN -> 0) or LeakyReLU composed as max-part + slope * min-part (NaN -> 0,
+// -0 -> +0), each step rounded in f32 like the reference's scalar expression.
+__device__ __forceinline__ float fused_apply(const EpiParams& e, float v, float bias) {
+    if (e.fbias_axis != AX_NONE) v = __fadd_rn(v, bias);
+    if (e.act == FACT_RELU) return v > 0.0f ? v : 0.0f;
+    if (e.act == FACT_LEAKY) {
+        const float hi = v > 0.0f ? v : 0.0f;
+        const float lo = v < 0.0f ? v : 0.0f;
+        return __fadd_rn(hi, __fmul_rn(e.leak, lo));
+    }
+    return v;
+}
+
 // Output stores: the local C and every mirror (same byte offset).
 __device__ __forceinline__ void out_v4(const EpiParams& e, int64_t byte_off, uint32_t a,
                                        uint32_t b, uint32_t c, uint32_t d) {
@@ -163,7 +177,8 @@ template <Out OUT, int CH>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t Nk,
                                                const EpiParams& e, int64_t obase, int64_t gc,
                                                const ColParam* cp, double r_se, double r_nms,
-                                               uint32_t r_ulo, uint32_t r_uhi, uint32_t r_bp) {
+                                               uint32_t r_ulo, uint32_t r_uhi, uint32_t r_bp,
+                                               float r_fbias = 0.0f) {
     const bool full_chunk = gc + CH <= Nk;
     if constexpr (OUT == Out::Q8 || OUT == Out::U8) {
         constexpr bool U8 = OUT == Out::U8;
@@ -255,6 +270,14 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t 
                     x2 = __fmaf_rn(be, __uint_as_float(cv.z), x2);
                     x3 = __fmaf_rn(be, __uint_as_float(cv.w), x3);
                 }
+                if (e.act != FACT_NONE || e.fbias_axis != AX_NONE) {
+                    const bool colb = e.fbias_axis == AX_N;
+                    const float* fb = e.fbias + gc + g * 4;
+                    x0 = fused_apply(e, x0, colb ? fb[0] : r_fbias);
+                    x1 = fused_apply(e, x1, colb ? fb[1] : r_fbias);
+                    x2 = fused_apply(e, x2, colb ? fb[2] : r_fbias);
+                    x3 = fused_apply(e, x3, colb ? fb[3] : r_fbias);
+                }
                 out_v4(e, (obase + gc + g * 4) * 4, __float_as_uint(x0), __float_as_uint(x1),
                        __float_as_uint(x2), __float_as_uint(x3));
             }
@@ -265,6 +288,8 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t 
                 const int64_t off = obase + (gc + i) * e.cso;
                 float x = al * __uint_as_float(v[i]);
                 if (be != 0.0f) x = __fmaf_rn(be, out[off], x);
+                if (e.act != FACT_NONE || e.fbias_axis != AX_NONE)
+                    x = fused_apply(e, x, e.fbias_axis == AX_N ? e.fbias[gc + i] : r_fbias);
                 out_1<float>(e, off, x);
             }
         }

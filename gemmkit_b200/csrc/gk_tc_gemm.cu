@@ -302,6 +302,8 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
             const int64_t gcol0 = static_cast<int64_t>(tn) * BN;
             const bool row_ok = grow < p.Mk;
             const ColParam* cp = cparams + acc * BN;
+            const float r_fb = (OUT == Out::F32 && e.fbias_axis == AX_M && row_ok)
+                                   ? e.fbias[grow] : 0.0f;
 
             if (col_params && !warp_wait(&pready[acc], aph, abort_flag, p.status,
                                          GK_DEV_TIMEOUT_EPILOGUE, tmo))
@@ -347,7 +349,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                 } else if (row_ok) {
                     epilogue_chunk<OUT, CH>(cur, p.Nk, e, obase, gcol0 + col_base + c * CH,
                                             cp + col_base + c * CH, r_se, r_nms, r_ulo, r_uhi,
-                                            r_bp);
+                                            r_bp, r_fb);
                 }
             }
             if (partial) {
@@ -400,7 +402,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                         if (row_ok)
                             epilogue_chunk<OUT, CH>(sum, p.Nk, e, obase, gcol0 + col_base + c * CH,
                                                     cp + col_base + c * CH, r_se, r_nms, r_ulo,
-                                                    r_uhi, r_bp);
+                                                    r_uhi, r_bp, r_fb);
                     }
                 }
             }

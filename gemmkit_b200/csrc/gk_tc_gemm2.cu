@@ -339,6 +339,8 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
             const int64_t gcol0 = static_cast<int64_t>(tn) * BN + c0;
             const bool row_ok = grow < p.Mk;
             const ColParam* cp = cparams + acc * BN;
+            const float r_fb = (OUT == Out::F32 && e.fbias_axis == AX_M && row_ok)
+                                   ? e.fbias[grow] : 0.0f;
             const int wcols = width / 2;  // columns per warp group
             const int col_base = cgroup * wcols;
             const int nch = wcols / CH;
@@ -384,7 +386,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
                 }
                 if (row_ok)
                     epilogue_chunk<OUT, CH>(cur, p.Nk, e, obase, gc, cp + col_base + c * CH, r_se,
-                                            r_nms, r_ulo, r_uhi, r_bp);
+                                            r_nms, r_ulo, r_uhi, r_bp, r_fb);
             }
             if (C::QUANT && t_next < n_items) commit(raw_next, acc ^ 1);
         }

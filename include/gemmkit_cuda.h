@@ -243,6 +243,28 @@ int gk_gemm_half_f32_batched_unchecked(gk_workspace *ws, int is_f16, size_t batc
                                        ptrdiff_t csc, ptrdiff_t c_bs, gk_parallelism par,
                                        gk_stream_t stream);
 
+/* ---- fused float epilogue on the half -> f32 GEMM ------------------------------------- */
+
+/* gemmkit's gemm_fused (gemmkit/src/api/fused.rs:149-176) computes act(alpha*A*B + beta*C +
+ * bias) for f32/f64 GEMMs: the bias per row (length m) or per column (length n), then ReLU or
+ * LeakyReLU(slope) (gemmkit/src/kernel/epilogue.rs:258-330). These entries give the bf16 /
+ * f16 -> f32 GEMM the same fused epilogue (gemmkit has none for half inputs): the unchecked
+ * tier takes gemm_fused_unchecked's (bias, bias_dim, has_bias, act) selectors, the checked
+ * tier validates the views like gk_gemm_half_f32 and the bias length like gemmkit. With k == 0
+ * or alpha == 0, C <- act(beta*C + bias) (gemmkit/src/dispatch/float.rs:671-676). */
+enum gk_act { GK_ACT_NONE = 0, GK_ACT_RELU = 1, GK_ACT_LEAKY_RELU = 2 };
+int gk_gemm_half_f32_fused_unchecked(gk_workspace *ws, int is_f16, size_t m, size_t k, size_t n,
+                                     float alpha, const uint16_t *a, ptrdiff_t rsa,
+                                     ptrdiff_t csa, const uint16_t *b, ptrdiff_t rsb,
+                                     ptrdiff_t csb, float beta, float *c, ptrdiff_t rsc,
+                                     ptrdiff_t csc, const float *bias, int bias_dim,
+                                     int has_bias, int act, float leak, gk_parallelism par,
+                                     gk_stream_t stream);
+int gk_gemm_half_f32_fused(gk_workspace *ws, int is_f16, float alpha, gk_matref a, gk_matref b,
+                           float beta, gk_matmut c, const float *bias, size_t bias_len,
+                           int bias_dim, int act, float leak, gk_parallelism par,
+                           gk_stream_t stream);
+
 /* ---- tuning (the gemmkit-tune profile mechanism, gemmkit/src/tuning.rs:592-621) ------- */
 
 /* Force the tile width (N of the MMA: 16, 32, 64, 128 or 256; 0 = automatic) for later

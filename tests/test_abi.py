@@ -253,3 +253,20 @@ def test_knobs_get_set_and_validation():
         for n in names:
             gk.knob_set(n, -1)  # drop the overrides
     assert {n: gk.knob_get(n) for n in names} == base
+
+
+def test_fused_bias_validation_without_gpu():
+    """The checked fused entry rejects a bias whose length does not follow its dimension,
+    before any device work."""
+    a = gk.MatRef.new((16, 6), 2, 3, 3, 1)
+    b = gk.MatRef.new((16, 12), 3, 4, 4, 1)
+    c = gk.MatMut.new((64, 8), 2, 4, 4, 1)
+    with pytest.raises(gk.GemmkitError, match="per-column bias length 3 does not match n = 4"):
+        gk.gemm_half_f32_fused(1.0, a, b, 0.0, c, bias=(128, 3), bias_dim=gk.AXIS_COL)
+    with pytest.raises(gk.GemmkitError, match="per-row bias length 4 does not match m = 2"):
+        gk.gemm_half_f32_fused(1.0, a, b, 0.0, c, bias=(128, 4), bias_dim=gk.AXIS_ROW)
+    lib = _lib.load()
+    rc = lib.gk_gemm_half_f32_fused_unchecked(None, 0, 2, 3, 4, 1.0, C.c_void_p(16), 3, 1,
+                                              C.c_void_p(16), 4, 1, 0.0, C.c_void_p(16), 4, 1,
+                                              None, 1, 0, 7, 0.0, _lib.Parallelism(0, 0), None)
+    assert rc == _lib.GK_EINVAL and b"unknown activation 7" in lib.gk_last_error()
