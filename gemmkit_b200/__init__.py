@@ -25,7 +25,7 @@ __all__ = [
     "prepack_rhs_i8", "prepack_rhs_i8_unchecked", "gemm_i8_packed_b", "gemm_i8_packed_b_unchecked",
     "gemm_i8_packed_b_requant", "gemm_i8_requant_batched", "gemm_i8_requant_batched_ptr",
     "gemm_half_f32", "gemm_bf16_f32_unchecked", "gemm_f16_f32_unchecked",
-    "gemm_half_f32_batched", "gemm_half_f32_fused", "Activation", "gemm_i8_noalloc_unchecked", "set_tile_n", "knob_names", "knob_get",
+    "gemm_half_f32_batched", "gemm_half_f32_fused", "Activation", "quantize_f32_i8", "gemm_i8_noalloc_unchecked", "set_tile_n", "knob_names", "knob_get",
     "knob_set", "device_status", "selftest_wait_timeout",
 ]
 
@@ -426,6 +426,15 @@ def gemm_half_f32_fused(alpha: float, a: MatRef, b: MatRef, beta: float, c: MatM
         _stream(stream)))
     if sync:
         _sync(stream)
+
+
+def quantize_f32_i8(rows, cols, x, rsx, csx, q, rsq, csq, scale: float = 1.0,
+                    zero_point: int = 0, row_scales=None, stream=None) -> None:
+    """Extension: f32 -> i8 activations (raw device pointers). Per-tensor scale / zero point,
+    or per-row symmetric scales written to `row_scales` (a device pointer) when given."""
+    _check(_lib.load().gk_quantize_f32_i8_unchecked(
+        rows, cols, C.c_void_p(x), rsx, csx, C.c_void_p(q), rsq, csq, float(scale),
+        int(zero_point), C.c_void_p(row_scales) if row_scales else None, _stream(stream)))
 
 
 def gemm_bf16_f32_unchecked(m, k, n, alpha, a, rsa, csa, b, rsb, csb, beta, c, rsc, csc,

@@ -1197,6 +1197,31 @@ int gk_gemm_half_f32_fused(gk_workspace* ws, int is_f16, float alpha, gk_matref 
                       act, leak, stream);
 }
 
+// ---- producer step: quantize f32 activations (extension) -----------------------------------
+
+int gk_quantize_f32_i8_unchecked(size_t rows, size_t cols, const float* x, ptrdiff_t rsx,
+                                 ptrdiff_t csx, int8_t* q, ptrdiff_t rsq, ptrdiff_t csq,
+                                 float scale, int32_t zero_point, float* row_scales,
+                                 gk_stream_t stream) {
+    if (rows == 0 || cols == 0) return GK_OK;
+    if (!x || !q) return set_err(GK_EINVAL, "gemmkit: null input or output");
+    if (!row_scales) {
+        int rc = check_scale_value(scale);
+        if (rc) return rc;
+        if (zero_point < -128 || zero_point > 127)
+            return set_err(GK_EINVAL, "gemmkit: i8 zero point %d out of range", zero_point);
+    }
+    int dev = 0;
+    int rc = check_device(&dev);
+    if (rc) return rc;
+    if (gk::launch_quantize_rows(x, rsx, csx, static_cast<int64_t>(rows),
+                                 static_cast<int64_t>(cols), q, rsq, csq, scale,
+                                 row_scales ? 0 : zero_point, row_scales,
+                                 static_cast<cudaStream_t>(stream)))
+        return set_err(GK_ECUDA, "gemmkit: quantize kernel launch failed");
+    return GK_OK;
+}
+
 // ---- mirrored outputs (extension) ----------------------------------------------------------
 
 static int set_mirrors(Job& j, void* const* mirrors, int nmirror) {

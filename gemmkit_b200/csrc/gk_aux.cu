@@ -228,6 +228,58 @@ int launch_requant_fill(void* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
+// ---- producer step: f32 activations -> i8 ------------------------------------------------
+// q = saturate_i8(zp + rne(f64(x) / f64(scale))) with a correctly rounded f64 division and
+// round-half-even to integer, in the f64 arithmetic of gemmkit's requant step (NaN -> zp).
+// Per-tensor: one scale; dynamic per-row: scale_r = max_j |x_rj| / 127 (f32 division; 1 for an
+// all-zero row), written to `scales`, zp = 0. One CTA of 256 threads per row.
+__device__ __forceinline__ int8_t quant_one(float x, float scale, int32_t zp) {
+    double q = __ddiv_rn(static_cast<double>(x), static_cast<double>(scale));
+    long long r = isnan(q) ? 0 : __double2ll_rn(q);  // saturating for |q| beyond 2^63
+    if (r > (1LL << 40)) r = 1LL << 40;
+    if (r < -(1LL << 40)) r = -(1LL << 40);
+    long long v = r + zp;
+    v = v < -128 ? -128 : (v > 127 ? 127 : v);
+    return static_cast<int8_t>(v);
+}
+
+__global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t rsx, int64_t csx,
+                                     int64_t cols, int8_t* __restrict__ q, int64_t rsq,
+                                     int64_t csq, float scale, int32_t zp, float* scales) {
+    const int64_t r = blockIdx.x;
+    const float* xr = x + r * rsx;
+    int8_t* qr = q + r * rsq;
+    float s = scale;
+    if (scales) {  // dynamic: the row's absolute maximum
+        __shared__ float red[8];
+        float mx = 0.0f;
+        for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) mx = fmaxf(mx, fabsf(xr[j * csx]));
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+            for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+            if (threadIdx.x == 0) red[0] = v;
+        }
+        __syncthreads();
+        const float amax = red[0];
+        s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+        if (threadIdx.x == 0) scales[r] = s;
+    }
+    for (int64_t j = threadIdx.x; j < cols; j += blockDim.x) qr[j * csq] = quant_one(xr[j * csx], s, zp);
+}
+
+int launch_quantize_rows(const float* x, int64_t rsx, int64_t csx, int64_t rows, int64_t cols,
+                         int8_t* q, int64_t rsq, int64_t csq, float scale, int32_t zp,
+                         float* scales, cudaStream_t st) {
+    if (rows == 0 || cols == 0) return 0;
+    if (rows > 0x7fffffffLL) return 1;
+    quantize_rows_kernel<<<static_cast<unsigned>(rows), 256, 0, st>>>(x, rsx, csx, cols, q, rsq,
+                                                                      csq, scale, zp, scales);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
 // Waits on an mbarrier that nothing arrives on; the bounded wait gives up after timeout_ns,
 // records GK_DEV_TIMEOUT_SELFTEST and the kernel returns normally.
 __global__ void selftest_timeout_kernel(uint64_t timeout_ns, unsigned int* status) {

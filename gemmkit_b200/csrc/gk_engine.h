@@ -160,6 +160,11 @@ int launch_fused_fill_f32(float* c, int64_t m, int64_t n, int64_t rsc, int64_t c
 int launch_requant_fill(void* c, int64_t m, int64_t n, int64_t rsc, int64_t csc, int64_t cbs,
                         int64_t batch, const EpiParams& e, cudaStream_t s);
 int launch_selftest_timeout(uint64_t timeout_ns, cudaStream_t s);
+// f32 -> i8 quantize of a rows x cols view (per-tensor `scale`/`zp`, or per-row scales written
+// to `scales` when it is not null).
+int launch_quantize_rows(const float* x, int64_t rsx, int64_t csx, int64_t rows, int64_t cols,
+                         int8_t* q, int64_t rsq, int64_t csq, float scale, int32_t zp,
+                         float* scales, cudaStream_t s);
 
 // Sets this thread's gk_last_error() text (gk_api.cu); returns `code`.
 int set_last_error(int code, const char* text);

@@ -265,6 +265,19 @@ int gk_gemm_half_f32_fused(gk_workspace *ws, int is_f16, float alpha, gk_matref 
                            int bias_dim, int act, float leak, gk_parallelism par,
                            gk_stream_t stream);
 
+/* ---- producer step: f32 activations -> i8 (no counterpart in gemmkit) ---------------- */
+
+/* Quantize a rows x cols f32 view (element (i, j) at x[i*rsx + j*csx]) into i8 (q[i*rsq +
+ * j*csq]), the step that feeds the requantizing GEMMs: q = saturate_i8(zp +
+ * round_half_even(f64(x) / f64(scale))) in f64, NaN -> zp. With row_scales == NULL one
+ * per-tensor scale / zero_point (scale must be finite and > 0, zp in [-128, 127], as
+ * gemmkit's requant checks them); otherwise each row gets scale_r = max |x_r| / 127 (1 for an
+ * all-zero row), written to row_scales[i], with zero point 0 (symmetric, per token). */
+int gk_quantize_f32_i8_unchecked(size_t rows, size_t cols, const float *x, ptrdiff_t rsx,
+                                 ptrdiff_t csx, int8_t *q, ptrdiff_t rsq, ptrdiff_t csq,
+                                 float scale, int32_t zero_point, float *row_scales,
+                                 gk_stream_t stream);
+
 /* ---- tuning (the gemmkit-tune profile mechanism, gemmkit/src/tuning.rs:592-621) ------- */
 
 /* Force the tile width (N of the MMA: 16, 32, 64, 128 or 256; 0 = automatic) for later

@@ -270,3 +270,15 @@ def test_fused_bias_validation_without_gpu():
                                               C.c_void_p(16), 4, 1, 0.0, C.c_void_p(16), 4, 1,
                                               None, 1, 0, 7, 0.0, _lib.Parallelism(0, 0), None)
     assert rc == _lib.GK_EINVAL and b"unknown activation 7" in lib.gk_last_error()
+
+
+def test_quantize_argument_errors_without_gpu():
+    lib = _lib.load()
+    rc = lib.gk_quantize_f32_i8_unchecked(2, 2, C.c_void_p(16), 2, 1, C.c_void_p(16), 2, 1,
+                                          -1.0, 0, None, None)
+    assert rc == _lib.GK_EINVAL
+    rc = lib.gk_quantize_f32_i8_unchecked(2, 2, C.c_void_p(16), 2, 1, C.c_void_p(16), 2, 1,
+                                          0.5, 200, None, None)
+    assert rc == _lib.GK_EINVAL and b"zero point 200" in lib.gk_last_error()
+    assert lib.gk_quantize_f32_i8_unchecked(0, 5, None, 0, 0, None, 0, 0, 1.0, 0, None,
+                                            None) == _lib.GK_OK
