@@ -294,6 +294,23 @@ class PackedRhs:
     def cols(self) -> int:
         return _lib.load().gk_packed_rhs_cols(self.h)
 
+    def to_bytes(self) -> bytes:
+        """Extension: the serialized packed B (header + device-ready bytes)."""
+        lib = _lib.load()
+        need = C.c_size_t()
+        _check(lib.gk_packed_rhs_serialize(self.h, None, 0, C.byref(need)))
+        buf = C.create_string_buffer(need.value)
+        _check(lib.gk_packed_rhs_serialize(self.h, buf, need.value, C.byref(need)))
+        return buf.raw
+
+    @staticmethod
+    def from_bytes(data: bytes, stream=None) -> "PackedRhs":
+        """Extension: a packed B loaded back from `to_bytes` output onto the current device."""
+        h = C.c_void_p()
+        _check(_lib.load().gk_packed_rhs_deserialize(data, len(data), _stream(stream),
+                                                     C.byref(h)))
+        return PackedRhs(h)
+
     def __del__(self):
         try:
             if getattr(self, "h", None) is not None and self.h.value:

@@ -69,6 +69,8 @@ SIGNATURES = {
     "gk_prepack_rhs_i8": (i32, [MatRefC, vp, C.POINTER(vp)]),
     "gk_packed_rhs_free": (None, [vp]),
     "gk_packed_rhs_rows": (sz, [vp]),
+    "gk_packed_rhs_serialize": (i32, [vp, vp, sz, C.POINTER(sz)]),
+    "gk_packed_rhs_deserialize": (i32, [vp, sz, vp, C.POINTER(vp)]),
     "gk_packed_rhs_cols": (sz, [vp]),
     "gk_gemm_i8_packed_b_unchecked": (i32, [vp, i32, sz, vp, pd, pd, vp, i32, vp, pd, pd,
                                             Parallelism, vp]),

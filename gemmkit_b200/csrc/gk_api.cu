@@ -921,6 +921,93 @@ void gk_packed_rhs_free(gk_packed_rhs* p) {
     delete p;
 }
 
+// Serialized form: a 64-byte little-endian header (magic "GKPACK01", k, n, k_pad, n_pad,
+// layout tag, payload bytes, zero padding) followed by the tiled buffer as it lies on the
+// device. The layout tag names the tiled layout, so a future layout change is refused on load.
+namespace {
+constexpr char kPackMagic[8] = {'G', 'K', 'P', 'A', 'C', 'K', '0', '1'};
+constexpr uint64_t kPackLayoutTiled128 = 1;  // 128-byte K blocks, rows 16-byte-chunk swizzled
+struct PackHeader {
+    char magic[8];
+    uint64_t k, n, k_pad, n_pad, layout, payload;
+    uint64_t pad[1];
+};
+static_assert(sizeof(PackHeader) == 64, "header size");
+}  // namespace
+
+int gk_packed_rhs_serialize(const gk_packed_rhs* p, void* out, size_t cap, size_t* needed) {
+    if (!p || !needed) return set_err(GK_EINVAL, "gemmkit: null packed handle or size pointer");
+    const size_t payload = (p->k && p->n) ? p->k_pad * p->n_pad : 0;
+    *needed = sizeof(PackHeader) + payload;
+    if (!out) return GK_OK;  // size query
+    if (cap < *needed)
+        return set_err(GK_EINVAL, "gemmkit: serialization buffer of %zu bytes, %zu needed", cap,
+                       *needed);
+    PackHeader h;
+    memset(&h, 0, sizeof(h));
+    memcpy(h.magic, kPackMagic, 8);
+    h.k = p->k;
+    h.n = p->n;
+    h.k_pad = p->k_pad;
+    h.n_pad = p->n_pad;
+    h.layout = kPackLayoutTiled128;
+    h.payload = payload;
+    memcpy(out, &h, sizeof(h));
+    if (payload) {
+        cudaError_t e = cudaMemcpy(static_cast<char*>(out) + sizeof(h), p->buf, payload,
+                                   cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return cuda_err(e, "packed serialization copy");
+        }
+    }
+    return GK_OK;
+}
+
+int gk_packed_rhs_deserialize(const void* in, size_t len, gk_stream_t stream,
+                              gk_packed_rhs** out) {
+    if (!out || !in) return set_err(GK_EINVAL, "gemmkit: null input or output pointer");
+    *out = nullptr;
+    PackHeader h;
+    if (len < sizeof(h)) return set_err(GK_EINVAL, "gemmkit: serialized packed B is truncated");
+    memcpy(&h, in, sizeof(h));
+    if (memcmp(h.magic, kPackMagic, 8) != 0)
+        return set_err(GK_EINVAL, "gemmkit: not a serialized packed B (bad magic)");
+    if (h.layout != kPackLayoutTiled128)
+        return set_err(GK_EINVAL, "gemmkit: serialized packed B has unknown layout %llu",
+                       static_cast<unsigned long long>(h.layout));
+    const uint64_t want_kp = (h.k + 127) / 128 * 128, want_np = (h.n + 255) / 256 * 256;
+    const uint64_t want_payload = (h.k && h.n) ? want_kp * want_np : 0;
+    if (h.k_pad != want_kp || h.n_pad != want_np || h.payload != want_payload ||
+        h.k > static_cast<uint64_t>(INT32_MAX / 2) || h.n > static_cast<uint64_t>(INT32_MAX))
+        return set_err(GK_EINVAL, "gemmkit: serialized packed B has inconsistent dimensions");
+    if (len < sizeof(h) + h.payload)
+        return set_err(GK_EINVAL, "gemmkit: serialized packed B is truncated");
+    int dev = 0;
+    int rc = check_device(&dev);
+    if (rc) return rc;
+    gk_packed_rhs* p = new gk_packed_rhs{dev, nullptr, h.k, h.n, h.k_pad, h.n_pad};
+    if (h.payload) {
+        cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&p->buf), h.payload);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            delete p;
+            return cuda_err(e, "packed deserialization allocation");
+        }
+        e = cudaMemcpyAsync(p->buf, static_cast<const char*>(in) + sizeof(h), h.payload,
+                            cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
+        if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) {  // complete before returning, like gk_prepack_rhs_i8
+            cudaGetLastError();
+            cudaFree(p->buf);
+            delete p;
+            return cuda_err(e, "packed deserialization copy");
+        }
+    }
+    *out = p;
+    return GK_OK;
+}
+
 size_t gk_packed_rhs_rows(const gk_packed_rhs* p) { return p ? p->k : 0; }
 size_t gk_packed_rhs_cols(const gk_packed_rhs* p) { return p ? p->n : 0; }
 

@@ -161,6 +161,15 @@ int gk_prepack_rhs_i8_unchecked(const int8_t *b, ptrdiff_t rsb, ptrdiff_t csb, s
 int gk_prepack_rhs_i8(gk_matref b, gk_stream_t stream, gk_packed_rhs **out);
 void gk_packed_rhs_free(gk_packed_rhs *p);
 size_t gk_packed_rhs_rows(const gk_packed_rhs *p); /* PackedRhs::rows (k) */
+/* No counterpart in gemmkit (its PackedRhs lives only in memory): store a packed B and load it
+ * back, so weights are packed once and later loaded device-ready. gk_packed_rhs_serialize
+ * writes a 64-byte header (magic "GKPACK01", k, n, padded dimensions, layout tag) plus the
+ * packed bytes into host memory `out` of `cap` bytes (out == NULL: only set *needed).
+ * gk_packed_rhs_deserialize checks the header (magic, layout, dimensions, length) and returns
+ * a new handle on the current device, complete when it returns. */
+int gk_packed_rhs_serialize(const gk_packed_rhs *p, void *out, size_t cap, size_t *needed);
+int gk_packed_rhs_deserialize(const void *in, size_t len, gk_stream_t stream,
+                              gk_packed_rhs **out);
 size_t gk_packed_rhs_cols(const gk_packed_rhs *p); /* PackedRhs::cols (n) */
 
 /* gemm_i8_packed_b_unchecked_with (gemmkit/src/api/packed.rs:609-680): C(i32) <- alpha *

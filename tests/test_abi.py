@@ -282,3 +282,24 @@ def test_quantize_argument_errors_without_gpu():
     assert rc == _lib.GK_EINVAL and b"zero point 200" in lib.gk_last_error()
     assert lib.gk_quantize_f32_i8_unchecked(0, 5, None, 0, 0, None, 0, 0, 1.0, 0, None,
                                             None) == _lib.GK_OK
+
+
+def test_packed_deserialize_rejects_bad_input_without_gpu():
+    """Header checks run before any device work."""
+    import struct
+    lib = _lib.load()
+    out = C.c_void_p()
+    assert lib.gk_packed_rhs_deserialize(b"short", 5, None, C.byref(out)) == _lib.GK_EINVAL
+    assert b"truncated" in lib.gk_last_error()
+    bad = b"NOTPACK!" + bytes(56)
+    assert lib.gk_packed_rhs_deserialize(bad, 64, None, C.byref(out)) == _lib.GK_EINVAL
+    assert b"bad magic" in lib.gk_last_error()
+    hdr = b"GKPACK01" + struct.pack("<7Q", 100, 10, 128, 256, 9, 128 * 256, 0)
+    assert lib.gk_packed_rhs_deserialize(hdr, 64, None, C.byref(out)) == _lib.GK_EINVAL
+    assert b"unknown layout 9" in lib.gk_last_error()
+    hdr = b"GKPACK01" + struct.pack("<7Q", 100, 10, 256, 256, 1, 256 * 256, 0)
+    assert lib.gk_packed_rhs_deserialize(hdr, 64, None, C.byref(out)) == _lib.GK_EINVAL
+    assert b"inconsistent dimensions" in lib.gk_last_error()
+    hdr = b"GKPACK01" + struct.pack("<7Q", 100, 10, 128, 256, 1, 128 * 256, 0)
+    assert lib.gk_packed_rhs_deserialize(hdr, 64 + 100, None, C.byref(out)) == _lib.GK_EINVAL
+    assert b"truncated" in lib.gk_last_error()

@@ -537,3 +537,25 @@ def test_pair_prepacked_batched_c4_shape():
         want = O.requant_matrix(a[e], bT[e].T, scales=scales[e], scale_axis="col",
                                 bias=bias[e], bias_axis="row", zp=128, out_u8=True)
         assert np.array_equal(got[e].T, want), e
+
+
+def test_packed_serialize_round_trip():
+    """A packed B stored and loaded back gives the same bytes and the same products."""
+    rng = np.random.default_rng(404)
+    m, k, n = 200, 300, 500
+    a = rand_i8(rng, (m, k), -127, 127)
+    bT = rand_i8(rng, (n, k), -127, 127)
+    scales = rng.uniform(1e-4, 1e-3, n).astype(np.float32)
+    want = O.requant_matrix(a, bT.T, scales=scales, scale_axis="col", zp=1)
+    packed = gk.prepack_rhs_i8(gk.MatRef.new(dev(bT), k, n, 1, k))
+    blob = packed.to_bytes()
+    assert blob[:8] == b"GKPACK01" and len(blob) == 64 + 384 * 512
+    loaded = gk.PackedRhs.from_bytes(blob)
+    assert (loaded.rows(), loaded.cols()) == (k, n)
+    assert loaded.to_bytes() == blob
+    da, dsc = dev(a), dev(scales)
+    req = gk.Requantize(gk.RequantScale.PerCol(dsc), 1)
+    for pk in (packed, loaded):
+        dc = empty(m * n, np.int8)
+        gk.gemm_i8_packed_b_requant(m, ptr(da), k, 1, pk, req, ptr(dc), n, 1)
+        assert np.array_equal(host(dc).reshape(m, n), want)
