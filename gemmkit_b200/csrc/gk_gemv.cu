@@ -63,7 +63,7 @@ struct GemvCfg {
     static constexpr int X_BYTES = NB * BKB;  // the NB activation rows of the same K block
     static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int CP_BYTES = NB * static_cast<int>(sizeof(ColParam));
+    static constexpr int CP_BYTES = NB * static_cast<int>(sizeof(ColParam) + 4);
     // N = 16: a 6-stage ring (110 KB) so that two CTAs fit on an SM, one of this call and one
     // of the next, which fills its ring while this one drains. Wider N need more registers than
     // two CTAs allow and keep one CTA with 8 stages.
@@ -133,6 +133,7 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 5);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     ColParam* cp = reinterpret_cast<ColParam*>(smem + C::RING_BYTES + C::BAR_BYTES);
+    uint32_t* cbias = reinterpret_cast<uint32_t*>(cp + NB);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -304,6 +305,7 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
                 c.bias_plus = static_cast<uint32_t>(cb) + 0x80000000u;
                 c.pad = 0;
                 cp[et] = c;
+                cbias[et] = c.bias_plus;
             }
             epi_bar_sync();
         }
@@ -346,12 +348,18 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
             if (lane == 0) mbar_arrive(&tempty[acc]);
             have = true;
             if (p.split > 1) break;  // one item; summed across the cluster below
-            if (row_ok) {
+            int qm = QM_GENERAL;
+            if constexpr (QUANT) qm = pick_quant_mode(e, r_se);
+            with_quant_mode<QUANT>(qm, [&](auto qm_tag) {
+                constexpr int QM = decltype(qm_tag)::value;
+                if (row_ok) {
 #pragma unroll
-                for (int c = 0; c < NCH; ++c)
-                    epilogue_chunk<OUT, CH>(v[c], p.Nk, e, grow * e.ldo, c * CH, cp + c * CH,
-                                            r_se, r_nms, r_ulo, r_uhi, r_bp, r_fb);
-            }
+                    for (int c = 0; c < NCH; ++c)
+                        epilogue_chunk<OUT, CH, QM>(v[c], p.Nk, e, grow * e.ldo, c * CH,
+                                                    cp + c * CH, cbias + c * CH, r_se, r_nms,
+                                                    r_ulo, r_uhi, r_bp, r_fb);
+                }
+            });
         }
     }
 
@@ -375,6 +383,8 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
                                   v[c][4 * g + 2], v[c][4 * g + 3]);
         }
         cluster_sync();
+        int qm = QM_GENERAL;
+        if (QUANT && warp >= 2 && rank == 0 && have) qm = pick_quant_mode(p.e, r_se);
         if (warp >= 2 && rank == 0 && have && grow < p.Mk) {
             for (int j = 1; j < p.split; ++j) {
                 const uint32_t* src = reinterpret_cast<const uint32_t*>(
@@ -390,10 +400,14 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
                                 __fadd_rn(__uint_as_float(v[c][i]), __uint_as_float(src[c * CH + i])));
                     }
             }
+            with_quant_mode<QUANT>(qm, [&](auto qm_tag) {
+                constexpr int QM = decltype(qm_tag)::value;
 #pragma unroll
-            for (int c = 0; c < NCH; ++c)
-                epilogue_chunk<OUT, CH>(v[c], p.Nk, p.e, grow * p.e.ldo, c * CH, cp + c * CH,
-                                        r_se, r_nms, r_ulo, r_uhi, r_bp, r_fb);
+                for (int c = 0; c < NCH; ++c)
+                    epilogue_chunk<OUT, CH, QM>(v[c], p.Nk, p.e, grow * p.e.ldo, c * CH,
+                                                cp + c * CH, cbias + c * CH, r_se, r_nms, r_ulo,
+                                                r_uhi, r_bp, r_fb);
+            });
         }
     }
 

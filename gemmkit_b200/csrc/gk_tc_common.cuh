@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "gk_engine.h"
 #include "gk_sm100.cuh"
 
@@ -58,6 +60,18 @@ __device__ __forceinline__ int requant_q(uint32_t acc, uint32_t bias_plus, doubl
     const double p = __fma_rn(d, se, nms);
     const double y = __dadd_rn(p, 6755399441055744.0);
     return __double2loint(y) + zp;
+}
+
+// requant_q without the clamp and with zp inside the rounding constant (magic = 1.5*2^52 + zp),
+// exact when the scale is at most 2^-9 and zp is even: |v| <= 2^31 then bounds |p| by 2^22, so
+// the rounded integer plus zp sits in the low word, and a tie of p + zp goes to the even
+// neighbour of p shifted by the even zp, the same integer as rne(p) + zp.
+__device__ __forceinline__ int requant_q_small(uint32_t acc, uint32_t bias_plus, double se,
+                                               double nms, double magic) {
+    const uint32_t u = acc + bias_plus;
+    const double d = __hiloint2double(0x43300000, static_cast<int>(u));
+    const double p = __fma_rn(d, se, nms);
+    return __double2loint(__dadd_rn(p, magic));
 }
 
 // Four values saturated to the output band and packed little-endian (x0 in the low byte).
@@ -171,16 +185,82 @@ __device__ __forceinline__ void out_1(const EpiParams& e, int64_t elem_off, T v)
     for (int i = 0; i < e.nmirror; ++i) static_cast<T*>(e.mirror[i])[elem_off] = v;
 }
 
+// Requantize paths an epilogue picks once per tile (uniform across the warp), so that the chunk
+// loop is straight-line code: the general path takes every axis, zero point and scale; the two
+// short ones take a per-row (or per-tensor) scale of at most 2^-9 with an even zero point
+// (requant_q_small), with the bias per column (compact array) or per row / none (register).
+enum QuantMode { QM_GENERAL = 0, QM_SMALL_COLB = 1, QM_SMALL_ROWB = 2 };
+
+// The quant mode of this warp's rows for the current tile; every lane of the warp calls it.
+__device__ __forceinline__ int pick_quant_mode(const EpiParams& e, double r_se) {
+    const bool small = __all_sync(0xffffffffu, r_se <= 0x1p-9);
+    if (e.scale_axis == AX_N || (e.zp & 1) != 0 || !small) return QM_GENERAL;
+    return e.bias_axis == AX_N ? QM_SMALL_COLB : QM_SMALL_ROWB;
+}
+
+// Calls f(std::integral_constant<int, QM>) for the runtime mode qm (quantized outputs only;
+// the other outputs take the general path), so that each mode's chunk loop is its own code.
+template <bool QUANT, typename F>
+__device__ __forceinline__ void with_quant_mode(int qm, F&& f) {
+    if constexpr (QUANT) {
+        if (qm == QM_SMALL_COLB)
+            f(std::integral_constant<int, QM_SMALL_COLB>{});
+        else if (qm == QM_SMALL_ROWB)
+            f(std::integral_constant<int, QM_SMALL_ROWB>{});
+        else
+            f(std::integral_constant<int, QM_GENERAL>{});
+    } else {
+        f(std::integral_constant<int, QM_GENERAL>{});
+    }
+}
+
 // The epilogue of one chunk of CH accumulator columns held by this thread (its row), starting
 // at column gc of the output; columns at or past Nk are not written.
-template <Out OUT, int CH>
+template <Out OUT, int CH, int QM = QM_GENERAL>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t Nk,
                                                const EpiParams& e, int64_t obase, int64_t gc,
-                                               const ColParam* cp, double r_se, double r_nms,
-                                               uint32_t r_ulo, uint32_t r_uhi, uint32_t r_bp,
+                                               const ColParam* cp, const uint32_t* cb,
+                                               double r_se, double r_nms, uint32_t r_ulo,
+                                               uint32_t r_uhi, uint32_t r_bp,
                                                float r_fbias = 0.0f) {
     const bool full_chunk = gc + CH <= Nk;
-    if constexpr (OUT == Out::Q8 || OUT == Out::U8) {
+    if constexpr ((OUT == Out::Q8 || OUT == Out::U8) && QM != QM_GENERAL) {
+        constexpr bool U8 = OUT == Out::U8;
+        const double magic = 6755399441055744.0 + static_cast<double>(e.zp);
+        int q[CH];
+        if constexpr (QM == QM_SMALL_COLB) {
+#pragma unroll
+            for (int g = 0; g < CH / 4; ++g) {
+                const uint4 bq = reinterpret_cast<const uint4*>(cb)[g];
+                q[4 * g + 0] = requant_q_small(v[4 * g + 0], bq.x, r_se, r_nms, magic);
+                q[4 * g + 1] = requant_q_small(v[4 * g + 1], bq.y, r_se, r_nms, magic);
+                q[4 * g + 2] = requant_q_small(v[4 * g + 2], bq.z, r_se, r_nms, magic);
+                q[4 * g + 3] = requant_q_small(v[4 * g + 3], bq.w, r_se, r_nms, magic);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) q[i] = requant_q_small(v[i], r_bp, r_se, r_nms, magic);
+        }
+        if (e.relu) {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) q[i] = max(q[i], e.lo);
+        }
+        uint32_t w[CH / 4];
+#pragma unroll
+        for (int g = 0; g < CH / 4; ++g)
+            w[g] = pack4_sat<U8>(q[4 * g], q[4 * g + 1], q[4 * g + 2], q[4 * g + 3]);
+        if (e.vec && full_chunk) {
+#pragma unroll
+            for (int g = 0; g < CH / 16; ++g)
+                out_v4(e, obase + gc + g * 16, w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i)
+                if (gc + i < Nk)
+                    out_1<uint8_t>(e, obase + (gc + i) * e.cso,
+                                   static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3))));
+        }
+    } else if constexpr (OUT == Out::Q8 || OUT == Out::U8) {
         constexpr bool U8 = OUT == Out::U8;
         int q[CH];
         if (e.scale_axis == AX_N) {

@@ -48,7 +48,7 @@ struct TileCfg {
     static constexpr int B_BYTES = BN * BKB;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr bool QUANT = (OUT == Out::Q8 || OUT == Out::U8);
-    static constexpr int CP_BYTES = QUANT ? 2 * BN * 32 : 0;  // column params, x2 buffers
+    static constexpr int CP_BYTES = QUANT ? 2 * BN * (32 + 4) : 0;  // column params, x2 buffers
     static constexpr int BAR_BYTES = 256;
     static constexpr int RAW_STAGES = (SMEM_LIMIT - 1024 - BAR_BYTES - CP_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = RAW_STAGES > 12 ? 12 : RAW_STAGES;
@@ -87,6 +87,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 7);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     ColParam* cparams = reinterpret_cast<ColParam*>(smem + STAGES * C::STAGE_BYTES + C::BAR_BYTES);
+    uint32_t* cbias = reinterpret_cast<uint32_t*>(cparams + 2 * BN);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -278,6 +279,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                     c.bias_plus = static_cast<uint32_t>(r.cbias) + 0x80000000u;
                     c.pad = 0;
                     cparams[buf * BN + et] = c;
+                    cbias[buf * BN + et] = c.bias_plus;
                 }
                 mbar_arrive(&pready[buf]);
             }
@@ -325,33 +327,41 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                 part = p.sk_part +
                        static_cast<int64_t>(w.tile - p.dp_tiles) * p.sk_maxc * (BM * BN) +
                        static_cast<int64_t>((warp - 2) * 32 + lane) * C::WCOLS;
+            // The requantize path for this tile's rows, then the chunk loop compiled for it.
             // Double-buffered TMEM reads: chunk c + 1 is in flight while chunk c is processed.
-            uint32_t va[32], vb[32];
-            tmem_ld_chunk<CH>(tbase, va);
+            int qm = QM_GENERAL;
+            if constexpr (C::QUANT) qm = pick_quant_mode(e, r_se);
+            auto chunks = [&](auto qm_tag) {
+                constexpr int QM = decltype(qm_tag)::value;
+                uint32_t va[32], vb[32];
+                tmem_ld_chunk<CH>(tbase, va);
 #pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-                uint32_t(&cur)[32] = (c & 1) ? vb : va;
-                uint32_t(&nxt)[32] = (c & 1) ? va : vb;
-                tmem_wait_ld();
-                reg_fence<CH>(cur);
-                if (c + 1 < NCH) {
-                    tmem_ld_chunk<CH>(tbase + (c + 1) * CH, nxt);
-                } else {
-                    tc_fence_before();
-                    mbar_arrive(&tempty[acc]);
-                }
-                if (partial) {
-                    uint32_t* dst = part + static_cast<int64_t>(w.slot) * (BM * BN) + c * CH;
+                for (int c = 0; c < NCH; ++c) {
+                    uint32_t(&cur)[32] = (c & 1) ? vb : va;
+                    uint32_t(&nxt)[32] = (c & 1) ? va : vb;
+                    tmem_wait_ld();
+                    reg_fence<CH>(cur);
+                    if (c + 1 < NCH) {
+                        tmem_ld_chunk<CH>(tbase + (c + 1) * CH, nxt);
+                    } else {
+                        tc_fence_before();
+                        mbar_arrive(&tempty[acc]);
+                    }
+                    if (partial) {
+                        uint32_t* dst = part + static_cast<int64_t>(w.slot) * (BM * BN) + c * CH;
 #pragma unroll
-                    for (int g = 0; g < CH / 4; ++g)
-                        st_global_v4(dst + 4 * g, cur[4 * g], cur[4 * g + 1], cur[4 * g + 2],
-                                     cur[4 * g + 3]);
-                } else if (row_ok) {
-                    epilogue_chunk<OUT, CH>(cur, p.Nk, e, obase, gcol0 + col_base + c * CH,
-                                            cp + col_base + c * CH, r_se, r_nms, r_ulo, r_uhi,
-                                            r_bp, r_fb);
+                        for (int g = 0; g < CH / 4; ++g)
+                            st_global_v4(dst + 4 * g, cur[4 * g], cur[4 * g + 1], cur[4 * g + 2],
+                                         cur[4 * g + 3]);
+                    } else if (row_ok) {
+                        epilogue_chunk<OUT, CH, QM>(cur, p.Nk, e, obase, gcol0 + col_base + c * CH,
+                                                    cp + col_base + c * CH,
+                                                    cbias + acc * BN + col_base + c * CH, r_se,
+                                                    r_nms, r_ulo, r_uhi, r_bp, r_fb);
+                    }
                 }
-            }
+            };
+            with_quant_mode<C::QUANT>(qm, chunks);
             if (partial) {
                 // Publish this slot, then count it; the last contributor of the region sums
                 // every slot in slot order (exact for integers, fixed order for floats).
@@ -401,8 +411,9 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                         }
                         if (row_ok)
                             epilogue_chunk<OUT, CH>(sum, p.Nk, e, obase, gcol0 + col_base + c * CH,
-                                                    cp + col_base + c * CH, r_se, r_nms, r_ulo,
-                                                    r_uhi, r_bp, r_fb);
+                                                    cp + col_base + c * CH,
+                                                    cbias + acc * BN + col_base + c * CH, r_se,
+                                                    r_nms, r_ulo, r_uhi, r_bp, r_fb);
                     }
                 }
             }

@@ -45,7 +45,7 @@ struct PairCfg {
     static constexpr int B_BYTES = (BN / 2) * BKB;  // this CTA's half of B
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr bool QUANT = (OUT == Out::Q8 || OUT == Out::U8);
-    static constexpr int CP_BYTES = QUANT ? 2 * BN * 32 : 0;
+    static constexpr int CP_BYTES = QUANT ? 2 * BN * (32 + 4) : 0;  // + compact bias_plus
     static constexpr int BAR_BYTES = 256;
     // 4-byte outputs keep a 4 KB tile per epilogue warp for mirrored (peer) stores
     static constexpr bool WIDE = (OUT == Out::I32 || OUT == Out::F32);
@@ -103,6 +103,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 7);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     ColParam* cparams = reinterpret_cast<ColParam*>(smem + STAGES * C::STAGE_BYTES + C::BAR_BYTES);
+    uint32_t* cbias = reinterpret_cast<uint32_t*>(cparams + 2 * BN);
     uint32_t* epi_stage = reinterpret_cast<uint32_t*>(smem + STAGES * C::STAGE_BYTES +
                                                       C::BAR_BYTES + C::CP_BYTES);
 
@@ -316,6 +317,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
                     c.bias_plus = static_cast<uint32_t>(r.cbias) + 0x80000000u;
                     c.pad = 0;
                     cparams[buf * BN + et] = c;
+                    cbias[buf * BN + et] = c.bias_plus;
                 }
                 mbar_arrive(&pready[buf]);
             }
@@ -359,35 +361,43 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
             const int64_t obase = static_cast<int64_t>(b) * e.obs + grow * e.ldo;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + col_base);
-            uint32_t va[32], vb[32];
-            tmem_ld_chunk<CH>(tbase, va);
-#pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-                if (c >= nch) break;
-                uint32_t(&cur)[32] = (c & 1) ? vb : va;
-                uint32_t(&nxt)[32] = (c & 1) ? va : vb;
-                tmem_wait_ld();
-                reg_fence<CH>(cur);
-                if (c + 1 < nch) {
-                    tmem_ld_chunk<CH>(tbase + (c + 1) * CH, nxt);
-                } else {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive_cluster(tempty_l + 8u * acc);
-                }
-                const int64_t gc = gcol0 + col_base + c * CH;
-                if constexpr (C::WIDE && CH == 32) {
-                    // mirrored full chunk: the whole warp stages it (conditions warp-uniform)
-                    if (e.nmirror > 0 && e.vec && gc + CH <= p.Nk) {
-                        epilogue_chunk_mirrored_wide<OUT>(cur, e, obase, gc, row_ok,
-                                                          epi_stage + (warp - 2) * 1024, lane);
-                        continue;
+            // the requantize path for this tile's rows, then the chunk loop compiled for it
+            int qm = QM_GENERAL;
+            if constexpr (C::QUANT) qm = pick_quant_mode(e, r_se);
+            auto chunks = [&](auto qm_tag) {
+                constexpr int QM = decltype(qm_tag)::value;
+                uint32_t va[32], vb[32];
+                tmem_ld_chunk<CH>(tbase, va);
+    #pragma unroll
+                for (int c = 0; c < NCH; ++c) {
+                    if (c >= nch) break;
+                    uint32_t(&cur)[32] = (c & 1) ? vb : va;
+                    uint32_t(&nxt)[32] = (c & 1) ? va : vb;
+                    tmem_wait_ld();
+                    reg_fence<CH>(cur);
+                    if (c + 1 < nch) {
+                        tmem_ld_chunk<CH>(tbase + (c + 1) * CH, nxt);
+                    } else {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive_cluster(tempty_l + 8u * acc);
                     }
+                    const int64_t gc = gcol0 + col_base + c * CH;
+                    if constexpr (C::WIDE && CH == 32) {
+                        // mirrored full chunk: the whole warp stages it (conditions warp-uniform)
+                        if (e.nmirror > 0 && e.vec && gc + CH <= p.Nk) {
+                            epilogue_chunk_mirrored_wide<OUT>(cur, e, obase, gc, row_ok,
+                                                              epi_stage + (warp - 2) * 1024, lane);
+                            continue;
+                        }
+                    }
+                    if (row_ok)
+                        epilogue_chunk<OUT, CH, QM>(cur, p.Nk, e, obase, gc, cp + col_base + c * CH,
+                                                cbias + acc * BN + col_base + c * CH, r_se,
+                                                r_nms, r_ulo, r_uhi, r_bp, r_fb);
                 }
-                if (row_ok)
-                    epilogue_chunk<OUT, CH>(cur, p.Nk, e, obase, gc, cp + col_base + c * CH, r_se,
-                                            r_nms, r_ulo, r_uhi, r_bp, r_fb);
-            }
+            };
+            with_quant_mode<C::QUANT>(qm, chunks);
             if (C::QUANT && t_next < n_items) commit(raw_next, acc ^ 1);
         }
     }
