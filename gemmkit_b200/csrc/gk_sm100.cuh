@@ -331,6 +331,16 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
                  : "memory");
 }
 
+// An arrival that publishes no memory writes: it does not wait for the thread's earlier global
+// stores to become visible cluster-wide, which a release arrival does. For "this TMEM
+// accumulator has been read": the reads are complete (tcgen05.wait::ld) and ordered before the
+// arrival by tcgen05.fence::before_thread_sync, and the waiting MMA warp reads nothing that the
+// arriving thread wrote.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t caddr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr)
+                 : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t caddr, uint32_t bytes) {
     asm volatile(
         "mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(caddr),

@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
                     } else {
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive_cluster(tempty_l + 8u * acc);
+                        if (lane == 0) mbar_arrive_cluster_relaxed(tempty_l + 8u * acc);
                     }
                     const int64_t gc = gcol0 + col_base + c * CH;
                     if constexpr (C::WIDE && CH == 32) {
