@@ -46,8 +46,8 @@ def load_peaks():
 # ---- clocks ---------------------------------------------------------------------------------
 
 # DRAM bytes of one launch of the C2 kernel (tc_gemm_pair_kernel<I8,Q8,256>), from the ncu
-# capture summarised in profiles/tc_gemm_pair_kernel_i8_requant_c2_4096.md: 33.68 MB read +
-# 0.046 MB written (A and B read once; C stays in L2 within the launch).
+# capture summarised in profiles/tc_gemm_pair_kernel_i8_requant_c2_4096.md: 33.698 MB read +
+# 0.016 MB written (A and B read once; C stays in L2 within the launch).
 C2_TRAFFIC_BYTES = 33_714_176
 
 
