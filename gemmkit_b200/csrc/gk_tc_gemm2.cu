@@ -34,12 +34,17 @@
 
 namespace gk {
 
-template <Out OUT, int BN>
+// EPI16: 16 epilogue warps (four column groups, 16-column TMEM chunks) instead of 8, for
+// quantized outputs whose K is one or two 128-byte blocks: the mainloop is then a few MMAs
+// per tile and the requantize epilogue is the whole kernel, so more warps hide its latency
+// (with a long K the 8-warp form is faster: the epilogue already hides behind the MMAs).
+template <Out OUT, int BN, bool EPI16 = false>
 struct PairCfg {
-    static constexpr int NEPI = 8;                  // epilogue warps per CTA
+    static constexpr int NEPI = EPI16 ? 16 : 8;     // epilogue warps per CTA
     static constexpr int THREADS = 64 + 32 * NEPI;
-    static constexpr int WCOLS = BN / 2;            // accumulator columns per epilogue warp
-    static constexpr int CH = 32;
+    static constexpr int NGROUPS = NEPI / 4;        // column groups (4 TMEM lane quarters each)
+    static constexpr int WCOLS = BN / NGROUPS;      // accumulator columns per epilogue warp
+    static constexpr int CH = EPI16 ? 16 : 32;
     static constexpr int NCH = WCOLS / CH;
     static constexpr int A_BYTES = BM * BKB;        // this CTA's 128 rows of A
     static constexpr int B_BYTES = (BN / 2) * BKB;  // this CTA's half of B
@@ -76,11 +81,11 @@ __device__ __forceinline__ void pair_item(int t, const GemmParams& p, int& tile,
     }
 }
 
-template <Kind KIND, Out OUT, int BN>
-__global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
+template <Kind KIND, Out OUT, int BN, bool EPI16 = false>
+__global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
-    using C = PairCfg<OUT, BN>;
+    using C = PairCfg<OUT, BN, EPI16>;
     constexpr int STAGES = C::STAGES;
     constexpr int CH = C::CH;
     constexpr int NCH = C::NCH;
@@ -271,7 +276,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
     } else {
         // ---------------- epilogue (warps 2 .. 9, both CTAs) ----------------
         const int q = warp & 3;
-        const int cgroup = (warp - 2) >> 2;  // which half of the item's columns this warp drains
+        const int cgroup = (warp - 2) >> 2;  // which column group of the item this warp drains
         const int et = threadIdx.x - 64;
         const EpiParams& e = p.e;
         const int row = q * 32 + lane;
@@ -343,7 +348,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
             const ColParam* cp = cparams + acc * BN;
             const float r_fb = (OUT == Out::F32 && e.fbias_axis == AX_M && row_ok)
                                    ? e.fbias[grow] : 0.0f;
-            const int wcols = width / 2;  // columns per warp group
+            const int wcols = width / C::NGROUPS;  // columns per warp group
             const int col_base = cgroup * wcols;
             const int nch = wcols / CH;
 
@@ -413,10 +418,10 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN>::THREADS, 1)
     }
 }
 
-template <Kind KIND, Out OUT, int BN>
+template <Kind KIND, Out OUT, int BN, bool EPI16 = false>
 static int launch_pair_one(const TcProblem& pr, const TcPlan& plan, GemmParams gp, char* err,
                            size_t errlen) {
-    using C = PairCfg<OUT, BN>;
+    using C = PairCfg<OUT, BN, EPI16>;
     constexpr int ES = (KIND == Kind::I8) ? 1 : 2;
     CUtensorMap ta, tb;
     int rc;
@@ -434,7 +439,7 @@ static int launch_pair_one(const TcProblem& pr, const TcPlan& plan, GemmParams g
     gp.b_tiled = pr.b.slab ? static_cast<const uint8_t*>(pr.b.ptr) : nullptr;
     gp.a_slab = pr.a.slab;
     gp.b_slab = pr.b.slab;
-    auto kern = tc_gemm_pair_kernel<KIND, OUT, BN>;
+    auto kern = tc_gemm_pair_kernel<KIND, OUT, BN, EPI16>;
     static int attr_done[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -514,6 +519,13 @@ int launch_pair(const TcProblem& pr, const TcPlan& plan, const GemmParams& gp, c
     if (pr.kind == K && pr.out == O)                                                     \
         return plan.bn == 256 ? launch_pair_one<K, O, 256>(pr, plan, gp, err, errlen)    \
                               : launch_pair_one<K, O, 128>(pr, plan, gp, err, errlen);
+    // quantized output with a one- or two-block K: the epilogue-bound form
+    if (pr.kind == Kind::I8 && plan.bn == 256 && plan.num_kb <= 2) {
+        if (pr.out == Out::Q8)
+            return launch_pair_one<Kind::I8, Out::Q8, 256, true>(pr, plan, gp, err, errlen);
+        if (pr.out == Out::U8)
+            return launch_pair_one<Kind::I8, Out::U8, 256, true>(pr, plan, gp, err, errlen);
+    }
     GK_PAIR_CASE(Kind::I8, Out::I32)
     GK_PAIR_CASE(Kind::I8, Out::Q8)
     GK_PAIR_CASE(Kind::I8, Out::U8)
