@@ -326,11 +326,6 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 }
 
 // Arrive on an mbarrier given by its shared::cluster address (own CTA or the peer).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr)
-                 : "memory");
-}
-
 // An arrival that publishes no memory writes: it does not wait for the thread's earlier global
 // stores to become visible cluster-wide, which a release arrival does. For "this TMEM
 // accumulator has been read": the reads are complete (tcgen05.wait::ld) and ordered before the
