@@ -21,6 +21,7 @@ from ._lib import (AXIS_COL, AXIS_NONE, AXIS_ROW, GK_EINVAL, GK_ENODEV, GK_ENOME
 __all__ = [
     "GemmkitError", "Parallelism", "MatRef", "MatMut", "Workspace", "RequantScale", "Requantize",
     "PackedRhs", "gemm_i8", "gemm_i8_with", "gemm_i8_unchecked", "gemm_i8_requant",
+    "gemv_i8_requant",
     "gemm_i8_requant_u8", "gemm_i8_requant_unchecked", "gemm_i8_requant_u8_unchecked",
     "prepack_rhs_i8", "prepack_rhs_i8_unchecked", "gemm_i8_packed_b", "gemm_i8_packed_b_unchecked",
     "gemm_i8_packed_b_requant", "gemm_i8_requant_batched", "gemm_i8_requant_batched_ptr",
@@ -360,6 +361,17 @@ def gemm_i8_packed_b_requant(m, a, rsa, csa, packed: PackedRhs, req: Requantize,
     r = req.c()
     _check(_lib.load().gk_gemm_i8_packed_b_requant_unchecked(
         _ws(ws), m, a, rsa, csa, packed.h, C.byref(r), c, rsc, csc, int(out_u8), par.c(),
+        _stream(stream)))
+
+
+def gemv_i8_requant(m, a, rsa, csa, packed: PackedRhs, req: Requantize, c, rsc, csc,
+                    out_u8=False, ws=None, stream=None) -> None:
+    """The decode-step GEMV: gemm_i8_packed_b_requant for 1 <= m <= 64 activation rows on the
+    small-M streaming kernel (gemmkit's internal small-shape route,
+    gemmkit/src/special/small_mn.rs:834-1060, given an entry of its own)."""
+    r = req.c()
+    _check(_lib.load().gk_gemv_i8_requant_unchecked(
+        _ws(ws), m, a, rsa, csa, packed.h, C.byref(r), c, rsc, csc, int(out_u8),
         _stream(stream)))
 
 

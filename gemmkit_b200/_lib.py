@@ -77,6 +77,8 @@ SIGNATURES = {
     "gk_gemm_i8_packed_b": (i32, [vp, i32, MatRefC, vp, i32, MatMutC, Parallelism, vp]),
     "gk_gemm_i8_packed_b_requant_unchecked": (i32, [vp, sz, vp, pd, pd, vp, C.POINTER(RequantC),
                                                     vp, pd, pd, C.c_int, Parallelism, vp]),
+    "gk_gemv_i8_requant_unchecked": (i32, [vp, sz, vp, pd, pd, vp, C.POINTER(RequantC), vp, pd,
+                                           pd, C.c_int, vp]),
     "gk_gemm_i8_requant_batched_unchecked": (i32, [vp, sz, sz, sz, sz, vp, pd, pd, pd, vp, pd,
                                                    pd, pd, C.POINTER(RequantC), pd, pd, vp, pd,
                                                    pd, pd, C.c_int, Parallelism, vp]),

@@ -1094,6 +1094,17 @@ int gk_gemm_i8_packed_b_requant_unchecked(gk_workspace* ws, size_t m, const int8
     return execute(j);
 }
 
+int gk_gemv_i8_requant_unchecked(gk_workspace* ws, size_t m, const int8_t* a, ptrdiff_t rsa,
+                                 ptrdiff_t csa, const gk_packed_rhs* packed,
+                                 const gk_requant* req, void* c, ptrdiff_t rsc, ptrdiff_t csc,
+                                 int out_u8, gk_stream_t stream) {
+    if (m < 1 || m > 64)
+        return set_err(GK_EINVAL, "gemmkit: gemv takes 1 to 64 activation rows (m = %zu)", m);
+    const gk_parallelism par{0, 0};
+    return gk_gemm_i8_packed_b_requant_unchecked(ws, m, a, rsa, csa, packed, req, c, rsc, csc,
+                                                 out_u8, par, stream);
+}
+
 // ---- batched ------------------------------------------------------------------------------
 
 int gk_gemm_i8_requant_batched_unchecked(gk_workspace* ws, size_t batch, size_t m, size_t k,

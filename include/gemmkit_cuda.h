@@ -193,6 +193,17 @@ int gk_gemm_i8_packed_b_requant_unchecked(gk_workspace *ws, size_t m, const int8
                                           void *c, ptrdiff_t rsc, ptrdiff_t csc, int out_u8,
                                           gk_parallelism par, gk_stream_t stream);
 
+/* The decode-step GEMV. gemmkit reaches its small-shape route only from inside dispatch
+ * (special/small_mn.rs:834-1060, gated at dispatch.rs:438-482); this entry names it:
+ * C = requant(A * packedB) for 1 <= m <= 64 activation rows, on the bandwidth-bound small-M
+ * kernel that streams the prepacked weights once from HBM (unless GEMMKIT_CUDA_GEMV=0).
+ * Arguments and results as gk_gemm_i8_packed_b_requant_unchecked; m outside [1, 64] is
+ * GK_EINVAL. */
+int gk_gemv_i8_requant_unchecked(gk_workspace *ws, size_t m, const int8_t *a, ptrdiff_t rsa,
+                                 ptrdiff_t csa, const gk_packed_rhs *packed,
+                                 const gk_requant *req, void *c, ptrdiff_t rsc, ptrdiff_t csc,
+                                 int out_u8, gk_stream_t stream);
+
 /* ---- batched (extension: gemmkit's batched entries are float-only, api/batched.rs:188) -- */
 
 /* Strided batch of independent requantized products, shaped as gemmkit's

@@ -303,3 +303,14 @@ def test_packed_deserialize_rejects_bad_input_without_gpu():
     hdr = b"GKPACK01" + struct.pack("<7Q", 100, 10, 128, 256, 1, 128 * 256, 0)
     assert lib.gk_packed_rhs_deserialize(hdr, 64 + 100, None, C.byref(out)) == _lib.GK_EINVAL
     assert b"truncated" in lib.gk_last_error()
+
+
+def test_gemv_entry_row_range():
+    """gk_gemv_i8_requant_unchecked takes 1 to 64 activation rows; checked before any device
+    work, so it needs no GPU."""
+    class _NoPack:
+        h = None
+    req = gk.Requantize(gk.RequantScale.PerTensor(0.01), 0)
+    for m in (0, 65):
+        expect_err(lambda: gk.gemv_i8_requant(m, 0, 1, 1, _NoPack(), req, 0, 1, 1),
+                   "gemv takes 1 to 64 activation rows")

@@ -152,3 +152,32 @@ def test_prepacked_narrow_b(shape):
     gk.gemm_i8_packed_b(2, gk.MatRef.from_row_major(dev(a), m, k), packed, 3,
                         gk.MatMut.from_col_major(dc, m, n))
     assert np.array_equal(gather(host(dc), m, n, 1, m), want)
+
+
+@pytest.mark.parametrize("M", [1, 4, 16, 64])
+@pytest.mark.parametrize("out_u8", [False, True])
+def test_gemv_entry(M, out_u8):
+    """gk_gemv_i8_requant_unchecked: bit-exact against the oracle and against the packed
+    requant entry on the same inputs (both C orientations)."""
+    k, n = 2048, 3000
+    rng = np.random.default_rng(M * 3 + out_u8)
+    a = rand_i8(rng, (M, k), -127, 127)
+    bT = rand_i8(rng, (n, k), -127, 127)
+    scales = rng.uniform(1e-4, 1e-3, n).astype(np.float32)
+    bias = rng.integers(-3000, 3000, n).astype(np.int32)
+    zp = 128 if out_u8 else -1
+    want = O.requant_matrix(a, bT.T, scales=scales, scale_axis="col", bias=bias,
+                            bias_axis="col", zp=zp, out_u8=out_u8)
+    packed = gk.prepack_rhs_i8(gk.MatRef.new(dev(bT), k, n, 1, k))
+    req = gk.Requantize(gk.RequantScale.PerCol(dev(scales)), zp, dev(bias), gk.AXIS_COL)
+    da = dev(a)
+    dt = np.uint8 if out_u8 else np.int8
+    for rsc, csc in ((n, 1), (1, M)):
+        dc = empty(M * n, dt)
+        gk.gemv_i8_requant(M, ptr(da), k, 1, packed, req, ptr(dc), rsc, csc, out_u8=out_u8)
+        got = gather(host(dc), M, n, rsc, csc)
+        assert np.array_equal(got, want)
+        dref = empty(M * n, dt)
+        gk.gemm_i8_packed_b_requant(M, ptr(da), k, 1, packed, req, ptr(dref), rsc, csc,
+                                    out_u8=out_u8)
+        assert np.array_equal(host(dc), host(dref))
