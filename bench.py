@@ -6,11 +6,20 @@ One step = one requantized i8 GEMM of BASELINE config 2 (A [4096 x 4096] i8 acti
 prepacked column-major B [4096 x 4096] i8 weights, per-column i32 bias and f32 scale, zero
 point 0, ReLU, i8 output) through the C ABI (gk_gemm_i8_packed_b_requant_unchecked). Inputs
 are seeded synthetic matrices with the config's distributions; 4 input sets rotate so the
-working set (4 x 48 MiB) exceeds the 126 MB L2. Under torchrun every rank runs its own
-problem (weak scaling, no collective on the data path); the time is the max over ranks.
+working set (4 x 48 MiB) exceeds the 126 MB L2. Under torchrun every rank runs its own C2
+problem for the headline (weak scaling); the time is the max over ranks.
+
+The same line carries the other BASELINE configs as extra keys, each with its own roofline:
+  c1, c3, c4           (one GPU: 1024^3 i8 -> i32, 8192^3 bf16 -> f32, batched requant u8);
+  gemv                 (config 5 at M = 1, 4, 16, CUDA-graph replay);
+  c3s_nvlink, c3s_nccl, c3s_local, c4s
+                       (under torchrun: config 3 column-sharded over the ranks with C
+                        replicated by the GEMM's own peer stores / by NCCL all-gather / not
+                        replicated, and config 4 batch-sharded; strong scaling, whole job).
 
 `--impl reference` times the CPU restatement of gemmkit's multithreaded VNNI path
-(oracle/gk_cpu_baseline.c) on this host's cores for the same metric, on a row sample.
+(oracle/gk_cpu_baseline.c) on this host's cores for the same metric on the full config 2
+problem.
 """
 from __future__ import annotations
 
@@ -45,10 +54,15 @@ def load_peaks():
 
 # ---- clocks ---------------------------------------------------------------------------------
 
-# DRAM bytes of one launch of the C2 kernel (tc_gemm_pair_kernel<I8,Q8,256>), from the ncu
-# capture summarised in profiles/tc_gemm_pair_kernel_i8_requant_c2_4096.md: 33.698 MB read +
-# 0.016 MB written (A and B read once; C stays in L2 within the launch).
+# DRAM bytes of one launch of the C2 kernel (tc_gemm_pair_kernel<I8,Q8,256>): dram__bytes_read.sum
+# + dram__bytes_write.sum of one capture by
+#   ncu --set full --clock-control none -k regex:tc_gemm_pair -s 3 -c 1 \
+#       python bench.py --config c2 --steps 3 --warmup 3
+# 33.698 MB read + 0.016 MB written (A and B read once; C stays in L2 within the launch).
 C2_TRAFFIC_BYTES = 33_714_176
+C2_TRAFFIC_SOURCE = ("dram__bytes_read.sum + dram__bytes_write.sum of one launch, from `ncu --set "
+                     "full --clock-control none -k regex:tc_gemm_pair -s 3 -c 1 python bench.py "
+                     "--config c2 --steps 3 --warmup 3`")
 
 
 class ClockSampler:
@@ -195,6 +209,10 @@ class C2:
     """4096^3 requantized GEMM with a prepacked column-major B."""
     name = "c2_gemm_i8_requant_4096"
     m = n = k = 4096
+
+    @classmethod
+    def ops_per_step(cls) -> float:
+        return 2.0 * cls.m * cls.n * cls.k
 
     def __init__(self, seed: int):
         import torch
@@ -451,10 +469,113 @@ def run_config(args, ws, rank, local):
                                        "peak_source": peaks["source"]}}), flush=True)
 
 
+def _c3s_inputs(g):
+    """Config 3 for column sharding: the same A, B and C on every rank (seeded), this rank's
+    block of B's columns kept resident, C column-major."""
+    import torch
+    m = n = k = 8192
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.randn(m * k, device="cuda", generator=gen).to(torch.bfloat16)
+    bT = torch.randn(n * k, device="cuda", generator=gen).to(torch.bfloat16)
+    c0 = torch.randn(m * n, device="cuda", generator=gen)
+    n0, n1 = g.col_range(n) if g else (0, n)
+    b_block = bT[n0 * k: n1 * k].clone()
+    del bT
+    return m, n, k, a, b_block, c0, n0, n1
+
+
+def measure_c3s(args, ws, g, peaks, variants=("nvlink", "nccl", "local")) -> dict:
+    """Config 3 (8192^3 bf16 -> f32, beta 0.5) column-sharded over the ranks (strong scaling:
+    the whole problem is fixed and split). Variants: C replicated on every rank by the GEMM's
+    own peer stores ("nvlink"), by a local GEMM plus NCCL all-gather ("nccl"), or each rank's
+    block left local ("local"). Returns {"c3s_<variant>": {...}}; times are CUDA events on each
+    rank's stream, max over ranks."""
+    import torch
+
+    import gemmkit_b200 as gk
+    m, n, k, a, b_block, c0, n0, n1 = _c3s_inputs(g)
+    if g:
+        c = g.replicated_empty(m * n, torch.float32)
+        c.tensor.copy_(c0)
+        g.fence()
+    else:
+        c = None
+        cbuf = c0.clone()
+    del c0
+    work = 2.0 * m * n * k
+    steps = max(args.steps, 10)
+    out = {}
+    for v in variants:
+        if not g and v != "local":
+            continue
+        replicate = v != "local"
+
+        def step(i, v=v, replicate=replicate):
+            if g:
+                g.gemm_half_f32_cols(m, k, n, 1.0, a.data_ptr(), k, 1, b_block.data_ptr(), 1, k,
+                                     0.5, c, replicate=replicate,
+                                     route="nccl" if v == "nccl" else "nvlink")
+            else:
+                gk.gemm_bf16_f32_unchecked(m, k, n, 1.0, a.data_ptr(), k, 1, b_block.data_ptr(),
+                                           1, k, 0.5, cbuf.data_ptr(), 1, m)
+        ms = time_steps(step, steps, max(args.warmup, 3), ws) / steps
+        val = work / (ms * 1e-3) / 1e12
+        out[f"c3s_{v}"] = {
+            "workload": "c3_gemm_bf16_f32_8192_column_sharded", "n_gpus": ws,
+            "scaling": "strong", "steps": steps, "ms_per_step": round(ms, 5),
+            "value": round(val, 2), "unit": "TFLOP/s", "replicate_c": replicate,
+            "route": {"nvlink": "fused peer stores from the GEMM epilogue (CUDA IPC, NVLink)",
+                      "nccl": "local GEMM + NCCL all-gather of the column blocks",
+                      "local": "no replication"}[v],
+            "columns_per_rank": n1 - n0,
+            "frac_of_n_gpu_bf16_peak": round(val / (ws * peaks["bf16_tflops"]), 4),
+            "peak_source": f"bf16_tflops of {peaks['source']} peaks x n_gpus"}
+    if g:
+        c.close()
+    return out
+
+
+def measure_c4s(args, ws, g, peaks) -> dict:
+    """Config 4 (512 x (512 x 512 x 128) i8, per-row bias, per-column scale, u8 zp 128)
+    batch-sharded over the ranks: batch elements [b0, b1) per rank with their bias / scales,
+    no collective (strong scaling, whole job; max over ranks)."""
+    import torch
+
+    import gemmkit_b200 as gk
+    B, m, n, k = 512, 512, 512, 128
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    a = torch.randint(-128, 128, (B * m * k,), dtype=torch.int8, device="cuda", generator=gen)
+    bT = torch.randint(-128, 128, (B * n * k,), dtype=torch.int8, device="cuda", generator=gen)
+    bias = torch.randint(-2**15, 2**15 + 1, (B * m,), dtype=torch.int32, device="cuda",
+                         generator=gen)
+    scales = (torch.rand(B * n, device="cuda", generator=gen) * 9e-4 + 1e-4).float()
+    req = gk.Requantize(gk.RequantScale.PerCol(scales), 128, bias, gk.AXIS_ROW)
+    cbuf = torch.empty(B * m * n, dtype=torch.uint8, device="cuda")
+
+    def step(i):
+        if g:
+            g.gemm_i8_requant_batched_shard(B, m, k, n, a.data_ptr(), k, 1, m * k, bT.data_ptr(),
+                                            1, k, n * k, req, m, n, cbuf.data_ptr(), 1, m, m * n,
+                                            True)
+        else:
+            gk.gemm_i8_requant_batched(B, m, k, n, a.data_ptr(), k, 1, m * k, bT.data_ptr(), 1, k,
+                                       n * k, req, m, n, cbuf.data_ptr(), 1, m, m * n,
+                                       out_u8=True)
+    steps = max(args.steps, 20)
+    ms = time_steps(step, steps, max(args.warmup, 3), ws) / steps
+    nbytes = B * (m * k + n * k + m * n + 4 * m + 4 * n)
+    val = nbytes / (ms * 1e-3) / 1e9
+    b0, b1 = g.batch_range(B) if g else (0, B)
+    return {"c4s": {"workload": "c4_batched_i8_requant_u8_batch_sharded", "n_gpus": ws,
+                    "scaling": "strong", "steps": steps, "ms_per_step": round(ms, 5),
+                    "value": round(val, 1), "unit": "GB/s", "batch_per_rank": b1 - b0,
+                    "collective": "none",
+                    "frac_of_n_gpu_hbm": round(val / (ws * peaks["hbm_gbs"]), 4),
+                    "peak_source": f"hbm_gbs of {peaks['source']} peaks x n_gpus"}}
+
+
 def run_sharded(args, ws, rank, local):
-    """BASELINE config 3 column-sharded (and config 4 batch-sharded) over the ranks: the whole
-    problem is fixed and split (strong scaling); `value` = the whole job's rate, timed on the
-    device and maxed over ranks. With one rank the problem runs unsharded on one GPU."""
+    """`--config c3s|c4s`: one sharded config on its own (its own JSON line)."""
     import torch
     torch.cuda.set_device(local)
     peaks = load_peaks()
@@ -463,90 +584,51 @@ def run_sharded(args, ws, rank, local):
         from gemmkit_b200.shard import ShardGroup
         g = ShardGroup()
     if args.config == "c3s":
-        replicate = bool(1 if args.replicate is None else args.replicate)
-        m = n = k = 8192
-        gen = torch.Generator(device="cuda").manual_seed(3)  # same A, B and C on every rank
-        a = torch.randn(m * k, device="cuda", generator=gen).to(torch.bfloat16)
-        bT = torch.randn(n * k, device="cuda", generator=gen).to(torch.bfloat16)
-        c0 = torch.randn(m * n, device="cuda", generator=gen)
-        n0, n1 = g.col_range(n) if g else (0, n)
-        b_block = bT[n0 * k: n1 * k].clone()  # this rank's weight columns stay resident
-        del bT
-        if g:
-            c = g.replicated_empty(m * n, torch.float32)
-            c.tensor.copy_(c0)
-            g.fence()
-        else:
-            c = None
-            cbuf = c0.clone()
-        del c0
-        import gemmkit_b200 as gk
-
-        def step(i, rep=replicate):
-            if g:
-                g.gemm_half_f32_cols(m, k, n, 1.0, a.data_ptr(), k, 1, b_block.data_ptr(), 1, k,
-                                     0.5, c, replicate=rep, route=args.route)
-            else:
-                gk.gemm_bf16_f32_unchecked(m, k, n, 1.0, a.data_ptr(), k, 1, b_block.data_ptr(),
-                                           1, k, 0.5, cbuf.data_ptr(), 1, m)
-        ms = time_steps(step, args.steps, args.warmup, ws) / args.steps
-        ms_local = ms
-        if g and replicate:
-            ms_local = time_steps(lambda i: step(i, False), args.steps, args.warmup, ws) / args.steps
-        work = 2.0 * m * n * k
-        unit, val = "TFLOP/s", work / (ms * 1e-3) / 1e12
-        extra = {"replicate": replicate, "route": args.route if (g and replicate) else None,
-                 "columns_per_rank": n1 - n0,
-                 "ms_per_step_without_replication": round(ms_local, 5),
-                 "tflops_without_replication": round(work / (ms_local * 1e-3) / 1e12, 2),
-                 "frac_of_n_gpu_bf16_peak": round(val / (ws * peaks["bf16_tflops"]), 4)}
-        if g:
-            c.close()
-        name = "c3_gemm_bf16_f32_8192_column_sharded"
+        res = measure_c3s(args, ws, g, peaks)
     else:
-        replicate = bool(0 if args.replicate is None else args.replicate)
-        B, m, n, k = 512, 512, 512, 128
-        gen = torch.Generator(device="cuda").manual_seed(4)
-        a = torch.randint(-128, 128, (B * m * k,), dtype=torch.int8, device="cuda", generator=gen)
-        bT = torch.randint(-128, 128, (B * n * k,), dtype=torch.int8, device="cuda", generator=gen)
-        bias = torch.randint(-2**15, 2**15 + 1, (B * m,), dtype=torch.int32, device="cuda",
-                             generator=gen)
-        scales = (torch.rand(B * n, device="cuda", generator=gen) * 9e-4 + 1e-4).float()
-        import gemmkit_b200 as gk
-        req = gk.Requantize(gk.RequantScale.PerCol(scales), 128, bias, gk.AXIS_ROW)
-        if g and replicate:
-            c = g.replicated_empty(B * m * n, torch.uint8)
-            cptr = c.ptr()
-        else:
-            c = None
-            cbuf = torch.empty(B * m * n, dtype=torch.uint8, device="cuda")
-            cptr = cbuf.data_ptr()
-
-        def step(i):
-            if g:
-                g.gemm_i8_requant_batched_shard(B, m, k, n, a.data_ptr(), k, 1, m * k,
-                                                bT.data_ptr(), 1, k, n * k, req, m, n, cptr, 1,
-                                                m, m * n, True, c=c, replicate=replicate,
-                                                route=args.route)
-            else:
-                gk.gemm_i8_requant_batched(B, m, k, n, a.data_ptr(), k, 1, m * k, bT.data_ptr(),
-                                           1, k, n * k, req, m, n, cptr, 1, m, m * n,
-                                           out_u8=True)
-        ms = time_steps(step, args.steps, args.warmup, ws) / args.steps
-        nbytes = B * (m * k + n * k + m * n + 4 * m + 4 * n)
-        unit, val = "GB/s", nbytes / (ms * 1e-3) / 1e9
-        b0, b1 = g.batch_range(B) if g else (0, B)
-        extra = {"replicate": replicate, "route": args.route if (g and replicate) else None,
-                 "batch_per_rank": b1 - b0,
-                 "frac_of_n_gpu_hbm": round(val / (ws * peaks["hbm_gbs"]), 4)}
-        if c is not None:
-            c.close()
-        name = "c4_batched_i8_requant_u8_batch_sharded"
+        res = measure_c4s(args, ws, g, peaks)
     if rank == 0:
-        print(json.dumps({"config": args.config, "workload": name, "value": round(val, 2),
-                          "unit": unit, "n_gpus": ws, "scaling": "strong",
-                          "ms_per_step": round(ms, 5), "steps": args.steps,
-                          "warmup": args.warmup, **extra}), flush=True)
+        for key, d in res.items():
+            print(json.dumps({"config": args.config, "key": key, **d}), flush=True)
+
+
+def measure_single(args, ws, peaks) -> dict:
+    """BASELINE configs 1, 3 and 4 on this rank's GPU, each with the roofline of its bound
+    (c1: CUDA-graph replay of 100 calls, the call rate of a launch-bound loop; c3, c4: eager
+    back-to-back calls). Times are CUDA events, max over ranks."""
+    import torch
+    out = {}
+    specs = (("c1", C1, "CUDA-graph replay of 100 calls (eager calls are host-bound)"),
+             ("c3", C3, "eager, back to back"), ("c4", C4, "eager, back to back"))
+    for key, cls, how in specs:
+        w = cls(7)
+        steps = max(args.steps, 20)
+        ms = time_steps(w.step, steps, max(args.warmup, 3), ws) / steps
+        eager_ms = ms
+        if key == "c1":
+            gms = graph_step_ms(w, 100, ws)
+            if gms is not None:
+                ms = gms
+        if w.unit == "GB/s":
+            kval = w.bytes / (ms * 1e-3) / 1e9
+            peak, psrc = peaks["hbm_gbs"], f"hbm_gbs of {peaks['source']} peaks"
+        else:
+            kval = w.work / (ms * 1e-3) / 1e12
+            mult = 2.0 if w.unit == "TOPS" else 1.0
+            peak = peaks["bf16_tflops"] * mult
+            psrc = (f"2 x bf16_tflops of {peaks['source']} peaks (dense int8 = 2 x dense bf16)"
+                    if mult == 2.0 else f"bf16_tflops of {peaks['source']} peaks")
+        out[key] = {"workload": w.name, "value": round(ws * kval, 2), "unit": w.unit,
+                    "steps": steps, "ms_per_step": round(ms, 5),
+                    "ms_per_step_eager": round(eager_ms, 5), "timing": how,
+                    "roofline": {"bound": w.bound, "achieved": round(kval, 2),
+                                 "peak": round(peak, 1), "unit": w.unit,
+                                 "frac": round(kval / peak, 4), "peak_source": psrc,
+                                 "algorithmic": (f"{w.work:.6g} ops" if w.unit != "GB/s"
+                                                 else f"{w.bytes} bytes")}}
+        del w
+        torch.cuda.empty_cache()
+    return out
 
 
 def time_steps(fn, steps: int, warmup: int, ws: int):
@@ -660,70 +742,79 @@ def e2e_pipelined_ms(w, steps: int, warmup: int, ws: int) -> float:
     return max_over_ranks(e0.elapsed_time(e1), ws) / steps
 
 
-def cpu_baseline_c2(budget_s: float = 8.0) -> dict:
-    """Oracle VNNI restatement (all host threads) on a row sample of config 2."""
+def c2_config() -> dict:
+    """The workload of the headline, identical in both arms' JSON lines."""
+    return {"workload": C2.name, "m": C2.m, "n": C2.n, "k": C2.k,
+            "b": "prepacked, column-major", "c": "column-major i8",
+            "epilogue": "per-col i32 bias + f32 scale, zp 0, ReLU",
+            "inputs": "A, B uniform [-127, 127]; bias uniform [-2^15, 2^15]; scale uniform "
+                      "[1e-4, 1e-3]",
+            "l2": f"GPU arm: {ROTATE} rotating input sets ({ROTATE * 48} MiB > 126 MB L2)"}
+
+
+def _c2_host_problem():
+    """Config 2 on the host for the CPU legs: the whole 4096^3 problem, B prepacked in
+    gemmkit's VNNI layout once (gemmkit's prepack_rhs_i8, outside the timed calls)."""
     import oracle as O
     rng = np.random.default_rng(0)
-    k = n = 4096
-    rows = 512
-    a = rng.integers(-127, 128, (rows, k), dtype=np.int8)
+    m = k = n = 4096
+    a = rng.integers(-127, 128, (m, k), dtype=np.int8)
     bT = rng.integers(-127, 128, (n, k), dtype=np.int8)
     bias = rng.integers(-2**15, 2**15 + 1, n).astype(np.int32)
     scales = rng.uniform(1e-4, 1e-3, n).astype(np.float32)
     pb = O.VnniPacked(bT.reshape(-1), 1, k, k, n)
-    c = np.empty(rows * n, np.int8)
+    c = np.empty(m * n, np.int8)
     req = dict(scales=scales, scale_axis="col", bias=bias, bias_axis="col", zp=0, relu=True)
+
+    def call():
+        O.vnni_requant_packed(O.View(a.reshape(-1), m, k, k, 1), pb, O.View(c, m, n, 1, m), **req)
+    return O, m, n, k, call
+
+
+def cpu_baseline_c2(budget_s: float = 10.0) -> dict:
+    """Oracle VNNI restatement (all host threads) on the whole config 2 problem, repeated for
+    about `budget_s` seconds (at most 50 calls)."""
+    O, m, n, k, call = _c2_host_problem()
+    call()  # first touch of the output and the thread pool
     times = []
     t_end = time.perf_counter() + budget_s
     while time.perf_counter() < t_end or len(times) < 3:
         t0 = time.perf_counter()
-        O.vnni_requant_packed(O.View(a.reshape(-1), rows, k, k, 1), pb,
-                              O.View(c, rows, n, 1, rows), **req)
+        call()
         times.append(time.perf_counter() - t0)
         if len(times) >= 50:
             break
     med = statistics.median(times)
-    tops = 2.0 * rows * n * k / med / 1e12
+    tops = 2.0 * m * n * k / med / 1e12
     return {"value": round(tops, 4), "unit": "TOPS", "cores": O.threads(),
             "kind": "port",
-            "sample": f"{rows} of 4096 rows of config 2 (512x4096x4096, prepacked B, per-col "
-                      f"bias+scale, ReLU), median of {len(times)} runs; C restatement of "
-                      f"gemmkit's AVX-512 VNNI path (vnni={O.has_vnni()})"}
+            "sample": f"the whole config 2 problem (4096x4096x4096, prepacked B, per-col "
+                      f"bias+scale, ReLU, i8 out) per call, median of {len(times)} calls; C "
+                      f"restatement of gemmkit's multithreaded AVX-512 VNNI path "
+                      f"(vnni={O.has_vnni()})"}
 
 
 def run_reference(args, ws, rank):
     if rank != 0:
         return
-    import oracle as O
-    rng = np.random.default_rng(0)
-    k = n = 4096
-    rows = 512
-    a = rng.integers(-127, 128, (rows, k), dtype=np.int8)
-    bT = rng.integers(-127, 128, (n, k), dtype=np.int8)
-    bias = rng.integers(-2**15, 2**15 + 1, n).astype(np.int32)
-    scales = rng.uniform(1e-4, 1e-3, n).astype(np.float32)
-    pb = O.VnniPacked(bT.reshape(-1), 1, k, k, n)
-    c = np.empty(rows * n, np.int8)
-    req = dict(scales=scales, scale_axis="col", bias=bias, bias_axis="col", zp=0, relu=True)
-    call = lambda: O.vnni_requant_packed(O.View(a.reshape(-1), rows, k, k, 1), pb,  # noqa: E731
-                                         O.View(c, rows, n, 1, rows), **req)
+    O, m, n, k, call = _c2_host_problem()
     for _ in range(args.warmup):
         call()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         call()
     dt = time.perf_counter() - t0
-    ops = 2.0 * rows * n * k * args.steps
+    ops = 2.0 * m * n * k * args.steps
     tops = ops / dt / 1e12
-    sample = (f"{rows} of 4096 rows of config 2 per step (512x4096x4096, prepacked B, per-col "
+    sample = (f"the whole config 2 problem per step (4096x4096x4096, prepacked B, per-col "
               f"bias+scale, ReLU, i8 out); C restatement of gemmkit's multithreaded AVX-512 VNNI "
-              f"path (vnni={O.has_vnni()}); gemmkit itself is Rust and not buildable here")
+              f"path (vnni={O.has_vnni()}) on {O.threads()} host threads; gemmkit itself is "
+              f"Rust and not buildable here")
     out = {"impl": "reference", "metric": METRIC, "value": round(tops, 4), "unit": "TOPS",
            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": round(dt * 1e3 / args.steps, 4), "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic",
-           "config": {"workload": "c2_gemm_i8_requant_4096 (row sample on host cores)",
-                      "m": rows, "n": n, "k": k, "parallelism": "host threads"},
+           "config": c2_config(), "parallelism": f"{O.threads()} host threads (rank 0 only)",
            "cpu_baseline": {"value": round(tops, 4), "unit": "TOPS", "cores": O.threads(),
                             "kind": "port", "sample": sample},
            "e2e": {"value": round(tops, 4), "unit": "TOPS", "h2d_bytes_per_step": 0,
@@ -748,21 +839,22 @@ def main():
     ap.add_argument("--config", default=None,
                     help="run one BASELINE config alone: c1, c2, c3, c4, c5 (M=16), c51, c54; "
                          "c3s / c4s: the column- / batch-sharded forms over the torchrun ranks")
-    ap.add_argument("--route", default="nvlink", choices=["nvlink", "nccl"],
-                    help="c3s/c4s: replicate C through the GEMM's peer stores or NCCL")
-    ap.add_argument("--replicate", type=int, default=None,
-                    help="c3s/c4s: 1 = every rank ends with the whole C (c3s default 1, c4s 0)")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the c1 / c3 / c4 (one GPU) and sharded (torchrun) extra keys")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
-    ws, rank, local = dist_setup()
     if args.impl == "reference":
-        run_reference(args, ws, rank)
-        if ws > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
+        # the CPU arm runs on rank 0 alone; under torchrun the other ranks exit at once
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")),
+                      int(os.environ.get("RANK", "0")))
         return
 
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # NCCL's own init lines show each communicator's rank count
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+    ws, rank, local = dist_setup()
     if args.config in ("c3s", "c4s"):
         run_sharded(args, ws, rank, local)
         if ws > 1:
@@ -783,15 +875,26 @@ def main():
 
     w = C2(seed=1234 + rank)
     launches_before = w.launches_per_step
-    sampler = ClockSampler(local) if rank == 0 else None
     for i in range(args.warmup):
         w.step(i)
     torch.cuda.synchronize()
     barrier(ws)
+    # Clock record: NVML samples every 10 ms from the start of a ~100 ms pre-roll of the same
+    # step (untimed, at the load of the timed region) through the end of the timed region, so
+    # the record holds several samples even when the timed region is ~1 ms.
+    est_ms = time_steps(w.step, 20, 0, 1) / 20
+    preroll = int(min(5000, max(0, 100.0 / max(est_ms, 1e-3))))
+    sampler = ClockSampler(local) if rank == 0 else None
+    barrier(ws)
     if sampler:
         sampler.start()
+    for i in range(preroll):
+        w.step(i)
     ms = time_steps(w.step, args.steps, 0, ws)
     clocks = sampler.stop() if sampler else None
+    if clocks is not None:
+        clocks["window"] = (f"{preroll} untimed steps (~{preroll * est_ms:.0f} ms) then the "
+                            f"{args.steps} timed steps")
     ms_step = ms / args.steps
     value = ws * w.ops / (ms_step * 1e-3) / 1e12
 
@@ -817,6 +920,8 @@ def main():
 
     e2e_ms = e2e_pipelined_ms(w, args.e2e_steps, 3, ws)
     e2e_value = ws * w.ops / (e2e_ms * 1e-3) / 1e12
+    del w
+    torch.cuda.empty_cache()
 
     gemv = None
     if not args.no_gemv:
@@ -833,39 +938,44 @@ def main():
             del g
         torch.cuda.empty_cache()
 
+    extra = {}
+    if not args.no_extra:
+        if ws == 1:
+            extra.update(measure_single(args, ws, peaks))
+        else:
+            from gemmkit_b200.shard import ShardGroup
+            grp = ShardGroup()
+            extra.update(measure_c3s(args, ws, grp, peaks))
+            torch.cuda.empty_cache()
+            extra.update(measure_c4s(args, ws, grp, peaks))
+            torch.cuda.empty_cache()
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
         cpu = cpu_baseline_c2()
 
     if rank == 0:
-        kernel_tops = w.ops / (ms_step * 1e-3) / 1e12
+        kernel_tops = C2.ops_per_step() / (ms_step * 1e-3) / 1e12
+        pair_on = os.environ.get("GEMMKIT_CUDA_PAIR", "1")[:1] != "0"
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "TOPS", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "i8",
             "data": "synthetic",
-            "config": {"workload": w.name, "m": w.m, "n": w.n, "k": w.k,
-                       "b": "prepacked, column-major", "c": "column-major i8",
-                       "epilogue": "per-col i32 bias + f32 scale, zp 0, ReLU",
-                       "l2": f"{ROTATE} rotating input sets ({ROTATE * 48} MiB > 126 MB L2)",
-                       "parallelism": f"weak: {ws} independent problems, one per GPU"},
+            "config": c2_config(),
+            "parallelism": f"weak: {ws} independent config-2 problems, one per GPU",
             "roofline": {"bound": "tensor", "achieved": round(kernel_tops, 2),
                          "peak": round(int8_peak, 1), "unit": "TOPS",
                          "frac": round(kernel_tops / int8_peak, 4),
-                         "traffic": C2_TRAFFIC_BYTES if not os.environ.get("GEMMKIT_CUDA_PAIR",
-                                                                          "1").startswith("0")
-                         else None,
-                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one "
-                                           "ncu capture of this kernel on this workload "
-                                           "(profiles/tc_gemm_pair_kernel_i8_requant_c2_4096.md)",
+                         "traffic": C2_TRAFFIC_BYTES if pair_on else None,
+                         "traffic_source": C2_TRAFFIC_SOURCE,
                          "peak_source": f"2 x bf16_tflops of {peaks['source']} peaks (B200 dense "
                                         f"int8 = 2 x dense bf16)",
-                         "kernel": ("tc_gemm_kernel<I8,Q8,256>"
-                                    if os.environ.get("GEMMKIT_CUDA_PAIR", "1")[:1] == "0"
-                                    else "tc_gemm_pair_kernel<I8,Q8,256>"),
-                         "algorithmic_ops": w.ops},
+                         "kernel": ("tc_gemm_pair_kernel<I8,Q8,256>" if pair_on
+                                    else "tc_gemm_kernel<I8,Q8,256>"),
+                         "algorithmic_ops": C2.ops_per_step()},
             "e2e": {"value": round(e2e_value, 2), "unit": "TOPS",
-                    "h2d_bytes_per_step": w.m * w.k, "d2h_bytes_per_step": w.m * w.n,
+                    "h2d_bytes_per_step": C2.m * C2.k, "d2h_bytes_per_step": C2.m * C2.n,
                     "ms_per_step": round(e2e_ms, 4),
                     "how": "public call per step with its pinned-host copy in and out, steps "
                            "pipelined over copy-in / compute / copy-out streams"},
@@ -874,6 +984,7 @@ def main():
             "sustained": sustained,
             "cpu_baseline": cpu,
             "gemv": gemv,
+            **extra,
         }
         print(json.dumps(out), flush=True)
     if ws > 1:

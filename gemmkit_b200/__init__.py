@@ -505,7 +505,8 @@ def gemm_i8_noalloc_unchecked(m, k, n, alpha, a, rsa, csa, b, rsb, csb, beta, c,
 # ---- misc -----------------------------------------------------------------------------------
 
 def set_tile_n(bn: int) -> None:
-    """Force the MMA tile width (16/32/64/128/256; 0 = automatic) on this thread."""
+    """Force the MMA tile width (16/32/64/128/192/256) on this thread; 0 drops the override
+    (the GEMMKIT_CUDA_BN knob, by default chosen per shape)."""
     _check(_lib.load().gk_set_tile_n(bn))
 
 

@@ -677,7 +677,7 @@ int gk_knob_set(const char* name, int64_t value) {
 int gk_set_tile_n(int bn) {
     if (!(bn == 0 || bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 192 || bn == 256))
         return set_err(GK_EINVAL, "gemmkit: tile width must be 0, 16, 32, 64, 128, 192 or 256");
-    g_tile_n = bn;
+    g_tile_n = bn == 0 ? -1 : bn;  // 0: no thread override, the GEMMKIT_CUDA_BN knob decides
     return GK_OK;
 }
 

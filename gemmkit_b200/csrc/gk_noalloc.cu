@@ -163,6 +163,8 @@ extern "C" int gk_gemm_i8_noalloc_unchecked(size_t m, size_t k, size_t n, int32_
     e.vec = (e.cso == 1) && !(reinterpret_cast<uintptr_t>(c) & 15) &&
             ((e.ldo * 4) % 16 == 0 || Mk == 1);
     gk::TcProblem pr;
+    memset(&pr, 0, sizeof(pr));  // no stream-K scratch (sk_* null), no launch overlap
+    pr.pdl = 0;
     pr.kind = gk::Kind::I8;
     pr.out = gk::Out::I32;
     pr.Mk = Mk;

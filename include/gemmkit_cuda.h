@@ -300,8 +300,9 @@ int gk_quantize_f32_i8_unchecked(size_t rows, size_t cols, const float *x, ptrdi
 
 /* ---- tuning (the gemmkit-tune profile mechanism, gemmkit/src/tuning.rs:592-621) ------- */
 
-/* Force the tile width (N of the MMA: 16, 32, 64, 128 or 256; 0 = automatic) for later
- * calls on this thread; the GEMMKIT_CUDA_BN environment knob sets the process default. */
+/* Force the tile width (N of the MMA: 16, 32, 64, 128, 192 or 256) for later calls on this
+ * thread; 0 drops this thread's override, so the process-wide GEMMKIT_CUDA_BN knob applies
+ * again (its default, 0, chooses the width per shape). */
 int gk_set_tile_n(int bn);
 
 /* The engine's knobs, the counterpart of gemmkit's tuning getters / setters

@@ -126,7 +126,7 @@ def test_i32_layouts_and_tails(alpha, beta, layout):
         assert np.array_equal(got, want), (layout, c_row)
 
 
-@pytest.mark.parametrize("bn", [16, 32, 64, 128, 256])
+@pytest.mark.parametrize("bn", [16, 32, 64, 128, 192, 256])
 def test_every_tile_width(bn):
     rng = np.random.default_rng(bn)
     m, k, n = 260, 300, 530
@@ -300,9 +300,23 @@ def test_requant_degenerate_k0_fixture():
     assert host(dc).reshape(n, m).T.tolist() == s["expect"]
 
 
+def _vnni_requant(a, bT, out_u8=False, **req):
+    """The oracle's restatement of gemmkit's VNNI requant path (bit-identical to the scalar
+    restatement for every axis mix, tests/test_oracle.py) on all host threads: row-major
+    a (m x k) times B = bT^T, returned row-major m x n."""
+    m, k = a.shape
+    n = bT.shape[0]
+    pb = O.VnniPacked(np.ascontiguousarray(bT).reshape(-1), 1, k, k, n)
+    c = np.empty(m * n, np.uint8 if out_u8 else np.int8)
+    O.vnni_requant_packed(O.View(np.ascontiguousarray(a).reshape(-1), m, k, k, 1), pb,
+                          O.View(c, m, n, 1, m), out_u8=out_u8, **req)
+    return c.reshape(n, m).T
+
+
 def test_c2_config_full_size():
     """4096^3, prepacked column-major B, per-column bias and scale, zp 0,
-    ReLU, i8 out. Oracle on a row sample; full-size properties on the rest."""
+    ReLU, i8 out. Every output against the oracle (gemmkit/tests/epilogue/requant.rs:34-98
+    checks every element too), plus the unpacked-B / row-major-C route against the same."""
     rng = np.random.default_rng(2)
     m = n = k = 4096
     a = rand_i8(rng, (m, k), -127, 127)
@@ -315,15 +329,16 @@ def test_c2_config_full_size():
     dc = empty(m * n, np.int8)
     gk.gemm_i8_packed_b_requant(m, ptr(da), k, 1, packed, req, ptr(dc), 1, m)
     got = host(dc).reshape(n, m).T
-    rows = np.sort(rng.choice(m, 64, replace=False))
-    want = O.requant_matrix(a[rows], bT.T, scales=scales, scale_axis="col", bias=bias,
-                            bias_axis="col", zp=0, relu=True)
-    assert np.array_equal(got[rows], want)
-    # property: the unpacked B and a row-major C give the same bytes
+    want = _vnni_requant(a, bT, scales=scales, scale_axis="col", bias=bias, bias_axis="col",
+                         zp=0, relu=True)
+    assert np.array_equal(got, want)
+    rows = np.sort(rng.choice(m, 8, replace=False))  # the scalar restatement on a few rows
+    assert np.array_equal(got[rows], O.requant_matrix(
+        a[rows], bT.T, scales=scales, scale_axis="col", bias=bias, bias_axis="col", zp=0,
+        relu=True))
     dc2 = empty(m * n, np.int8)
     gk.gemm_i8_requant_ex_unchecked(m, k, n, ptr(da), k, 1, ptr(dbT), 1, k, req, ptr(dc2), n, 1)
-    assert np.array_equal(host(dc2).reshape(m, n), got)
-    assert got.min() >= 0  # ReLU with zp 0
+    assert np.array_equal(host(dc2).reshape(m, n), want)
 
 
 @pytest.mark.parametrize("M", [1, 4, 16])
@@ -351,9 +366,10 @@ def _c4_inputs(rng, batch, m, n, k):
     return a, bT, bias, scales
 
 
-@pytest.mark.parametrize("batch,sample", [(6, None), (512, 12)])
-def test_c4_batched(batch, sample):
-    """batch of (512x512x128), per-row bias, per-column scale, u8 zp 128."""
+@pytest.mark.parametrize("batch", [6, 512])
+def test_c4_batched(batch):
+    """batch of (512x512x128), per-row bias, per-column scale, u8 zp 128.
+    Every element of every batch member against the oracle."""
     rng = np.random.default_rng(batch)
     m = n = 512
     k = 128
@@ -364,11 +380,14 @@ def test_c4_batched(batch, sample):
     gk.gemm_i8_requant_batched(batch, m, k, n, ptr(da), k, 1, m * k, ptr(dbT), 1, k, n * k, req,
                                m, n, ptr(dc), 1, m, m * n, out_u8=True)
     got = host(dc).reshape(batch, n, m)
-    elems = range(batch) if sample is None else rng.choice(batch, sample, replace=False)
-    for e in elems:
-        want = O.requant_matrix(a[e], bT[e].T, scales=scales[e], scale_axis="col",
-                                bias=bias[e], bias_axis="row", zp=128, out_u8=True)
+    for e in range(batch):
+        want = _vnni_requant(a[e], bT[e], scales=scales[e], scale_axis="col", bias=bias[e],
+                             bias_axis="row", zp=128, out_u8=True)
         assert np.array_equal(got[e].T, want), e
+    e = batch - 1  # and the scalar restatement on one member
+    assert np.array_equal(got[e].T, O.requant_matrix(
+        a[e], bT[e].T, scales=scales[e], scale_axis="col", bias=bias[e], bias_axis="row",
+        zp=128, out_u8=True))
 
 
 def test_batched_ptr_array_matches_strided():

@@ -10,6 +10,7 @@ import pytest
 
 import gemmkit_b200 as gk
 from gemmkit_b200 import _lib
+import oracle as O
 from gpu_util import dev, host, rand_i8
 
 pytestmark = pytest.mark.gpu
@@ -60,8 +61,11 @@ def test_noalloc_matches_existing_entry_two_calls_in_a_row():
             free_before = torch.cuda.mem_get_info()[0]
     torch.cuda.synchronize()
     assert torch.cuda.mem_get_info()[0] == free_before  # no device memory taken by call 2
-    for dref, (_, dout, _) in zip(refs, outs):
-        assert np.array_equal(host(dout), host(dref))  # integer path: bit-exact
+    for (m, k, n), (a, b, c0), dref, (_, dout, _) in zip(shapes, inputs, refs, outs):
+        got = host(dout).reshape(m, n)
+        assert np.array_equal(got, host(dref).reshape(m, n))  # integer path: bit-exact
+        want = O.gemm_i8_matrix(3, a[:, :k], b, -2, c0)  # the CPU oracle (gemmkit's semantics)
+        assert np.array_equal(got, want)
     assert gk.device_status(0) == 0
 
 
