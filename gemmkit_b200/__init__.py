@@ -26,7 +26,7 @@ __all__ = [
     "prepack_rhs_i8", "prepack_rhs_i8_unchecked", "gemm_i8_packed_b", "gemm_i8_packed_b_unchecked",
     "gemm_i8_packed_b_requant", "gemm_i8_requant_batched", "gemm_i8_requant_batched_ptr",
     "gemm_half_f32", "gemm_bf16_f32_unchecked", "gemm_f16_f32_unchecked",
-    "gemm_half_f32_batched", "gemm_half_f32_fused", "Activation", "quantize_f32_i8", "gemm_i8_noalloc_unchecked", "set_tile_n", "knob_names", "knob_get",
+    "gemm_half_f32_batched", "gemm_half_f32_fused", "gemm_i8_fused", "gemm_i8_fused_unchecked", "Activation", "quantize_f32_i8", "gemm_i8_noalloc_unchecked", "set_tile_n", "knob_names", "knob_get",
     "knob_set", "device_status", "selftest_wait_timeout",
 ]
 
@@ -455,6 +455,31 @@ def gemm_half_f32_fused(alpha: float, a: MatRef, b: MatRef, beta: float, c: MatM
         _stream(stream)))
     if sync:
         _sync(stream)
+
+
+def gemm_i8_fused(alpha: int, a: MatRef, b: MatRef, beta: int, c: MatMut, bias=None,
+                  bias_dim: int = AXIS_ROW, act: Optional[Activation] = None,
+                  par: Parallelism = SERIAL, ws=None, stream=None, sync: bool = True) -> None:
+    """The i8 -> i32 GEMM with a fused integer epilogue (extension; gemmkit's gemm_fused is
+    float-only): C <- act(alpha*A*B + beta*C + bias), wrapping i32 arithmetic, the i32 bias
+    per row (AXIS_ROW, length m) or per column (AXIS_COL, length n), act None or ReLU."""
+    bp, bn = _flat(bias) if bias is not None else (0, 0)
+    _check(_lib.load().gk_gemm_i8_fused(
+        _ws(ws), int(alpha), a.c(), b.c(), int(beta), c.c(), C.c_void_p(bp or None), bn,
+        bias_dim, act.kind if act else _lib.ACT_NONE, par.c(), _stream(stream)))
+    if sync:
+        _sync(stream)
+
+
+def gemm_i8_fused_unchecked(m, k, n, alpha, a, rsa, csa, b, rsb, csb, beta, c, rsc, csc,
+                            bias=None, bias_dim: int = AXIS_ROW, act: int = 0,
+                            par: Parallelism = SERIAL, ws=None, stream=None) -> None:
+    """Raw-pointer tier of gemm_i8_fused (device pointers as ints; bias a device pointer or
+    None; act one of _lib.ACT_NONE / _lib.ACT_RELU)."""
+    _check(_lib.load().gk_gemm_i8_fused_unchecked(
+        _ws(ws), m, k, n, alpha, a, rsa, csa, b, rsb, csb, beta, c, rsc, csc,
+        C.c_void_p(bias) if bias else None, bias_dim, 1 if bias else 0, act, par.c(),
+        _stream(stream)))
 
 
 def quantize_f32_i8(rows, cols, x, rsx, csx, q, rsq, csq, scale: float = 1.0,

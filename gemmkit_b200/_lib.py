@@ -110,6 +110,10 @@ SIGNATURES = {
                                                C.c_int, f32, Parallelism, vp]),
     "gk_gemm_half_f32_fused": (i32, [vp, C.c_int, f32, MatRefC, MatRefC, f32, MatMutC, vp, sz,
                                      C.c_int, C.c_int, f32, Parallelism, vp]),
+    "gk_gemm_i8_fused_unchecked": (i32, [vp, sz, sz, sz, i32, vp, pd, pd, vp, pd, pd, i32, vp, pd,
+                                         pd, vp, C.c_int, C.c_int, C.c_int, Parallelism, vp]),
+    "gk_gemm_i8_fused": (i32, [vp, i32, MatRefC, MatRefC, i32, MatMutC, vp, sz, C.c_int, C.c_int,
+                               Parallelism, vp]),
     "gk_quantize_f32_i8_unchecked": (i32, [sz, sz, vp, pd, pd, vp, pd, pd, f32, i32, vp, vp]),
     "gk_set_tile_n": (i32, [C.c_int]),
     "gk_knob_names": (C.c_char_p, []),

@@ -85,10 +85,14 @@ int check_device(int* dev_out) {
 //   GEMMKIT_CUDA_GEMV     1 = streaming small-M kernel for Nk <= 64
 //   GEMMKIT_CUDA_PDL      1 = programmatic dependent launch (overlap with the previous kernel)
 //   GEMMKIT_CUDA_STREAMK  1 = stream-K tail for the last wave of the one-CTA kernel
-enum KnobId { K_BN = 0, K_PAIR, K_GEMV, K_PDL, K_STREAMK, K_COUNT };
-const char* const kKnobEnv[K_COUNT] = {"GEMMKIT_CUDA_BN", "GEMMKIT_CUDA_PAIR", "GEMMKIT_CUDA_GEMV",
-                                       "GEMMKIT_CUDA_PDL", "GEMMKIT_CUDA_STREAMK"};
-const int64_t kKnobDefault[K_COUNT] = {0, 1, 1, 1, 0};
+//   GEMMKIT_CUDA_GEMV_SK  1 = the small-M kernel splits its weight stream evenly over all SMs
+//                         (stream-K partials in the workspace) when whole tiles would not;
+//                         off by default (measured slower than whole tiles on config 5)
+enum KnobId { K_BN = 0, K_PAIR, K_GEMV, K_PDL, K_STREAMK, K_GEMVSK, K_COUNT };
+const char* const kKnobEnv[K_COUNT] = {"GEMMKIT_CUDA_BN",   "GEMMKIT_CUDA_PAIR",
+                                       "GEMMKIT_CUDA_GEMV", "GEMMKIT_CUDA_PDL",
+                                       "GEMMKIT_CUDA_STREAMK", "GEMMKIT_CUDA_GEMV_SK"};
+const int64_t kKnobDefault[K_COUNT] = {0, 1, 1, 1, 0, 0};
 std::atomic<int64_t> g_knob_set[K_COUNT];  // value + 1; 0 = no run-time override
 
 bool knob_valid(int id, int64_t v) {
@@ -129,6 +133,7 @@ bool streamk_enabled() { return knob(K_STREAMK) == 1; }
 bool pair_enabled() { return knob(K_PAIR) == 1; }
 bool gemv_enabled() { return knob(K_GEMV) == 1; }
 bool pdl_enabled() { return knob(K_PDL) == 1; }
+bool gemv_sk_enabled() { return knob(K_GEMVSK) == 1; }
 
 int tile_n_override() {
     if (g_tile_n >= 0) return g_tile_n;
@@ -426,6 +431,14 @@ int execute(const Job& j) {
     if ((j.k == 0 || alpha_zero) && j.nmirror > 0)
         return set_err(GK_EINVAL, "gemmkit: mirrored outputs need k > 0 and a nonzero alpha");
     if (j.k == 0 || alpha_zero) {
+        if (j.out == gk::Out::I32 && (j.act != GK_ACT_NONE || j.bias)) {
+            gk::EpiParams fe = e;
+            fe.bias_axis = map_axis(j.bias ? j.bias_axis : GK_AXIS_NONE, false);
+            fe.act = j.act;
+            rc = gk::launch_fused_fill_i32(static_cast<int32_t*>(j.c), j.m, j.n, j.rsc, j.csc,
+                                           j.beta_i, fe, j.stream);
+            return rc ? set_err(GK_ECUDA, "gemmkit: fill kernel launch failed") : GK_OK;
+        }
         if (j.out == gk::Out::I32) {
             for (int64_t b = 0; b < j.batch; ++b) {
                 rc = gk::launch_scale_c_i32(static_cast<int32_t*>(j.c) + b * j.cbs, j.m, j.n,
@@ -525,7 +538,8 @@ int execute(const Job& j) {
     pr.a.slab = ka.slab;
     pr.b.slab = kb.slab;
     gk::TcPlan plan;
-    gk::plan_tc_gemm2(pr, streamk_enabled(), pair_enabled(), gemv_enabled(), &plan);
+    gk::plan_tc_gemm2(pr, streamk_enabled(), pair_enabled(), gemv_enabled(), &plan,
+                      gemv_sk_enabled());
     const int64_t part_bytes = round_up(plan.part_words * 4, 256);
 
     gk_workspace* ws = j.ws ? j.ws : default_ws(dev);
@@ -649,7 +663,7 @@ void gk_workspace_free(gk_workspace* ws) {
 
 const char* gk_knob_names(void) {
     return "GEMMKIT_CUDA_BN,GEMMKIT_CUDA_PAIR,GEMMKIT_CUDA_GEMV,GEMMKIT_CUDA_PDL,"
-           "GEMMKIT_CUDA_STREAMK";
+           "GEMMKIT_CUDA_STREAMK,GEMMKIT_CUDA_GEMV_SK";
 }
 
 int gk_knob_get(const char* name, int64_t* value) {
@@ -715,6 +729,74 @@ int gk_gemm_i8(gk_workspace* ws, int32_t alpha, gk_matref a, gk_matref b, int32_
                                 static_cast<const int8_t*>(a.data), a.rs, a.cs,
                                 static_cast<const int8_t*>(b.data), b.rs, b.cs, beta,
                                 static_cast<int32_t*>(c.data), c.rs, c.cs, par, stream);
+}
+
+// ---- fused i32 epilogue (extension: gemmkit's gemm_fused is float-only) ---------------------
+
+static int i8_fused(gk_workspace* ws, size_t m, size_t k, size_t n, int32_t alpha,
+                    const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa, const int8_t* b, ptrdiff_t rsb,
+                    ptrdiff_t csb, int32_t beta, int32_t* c, ptrdiff_t rsc, ptrdiff_t csc,
+                    const int32_t* bias, int bias_dim, int has_bias, int act,
+                    gk_stream_t stream) {
+    if (m && n && !c) return set_err(GK_EINVAL, "gemmkit: null C");
+    if (m && n && k && alpha && (!a || !b)) return set_err(GK_EINVAL, "gemmkit: null A or B");
+    if (act == GK_ACT_LEAKY_RELU)
+        return set_err(GK_EINVAL,
+                       "gemmkit: the i32 fused epilogue has no LeakyReLU (its slope is a float)");
+    if (act != GK_ACT_NONE && act != GK_ACT_RELU)
+        return set_err(GK_EINVAL, "gemmkit: unknown activation %d", act);
+    if (has_bias && bias_dim != GK_AXIS_ROW && bias_dim != GK_AXIS_COL)
+        return set_err(GK_EINVAL, "gemmkit: bias dimension must be row or column");
+    if (has_bias && m && n && !bias) return set_err(GK_EINVAL, "gemmkit: null bias");
+    Job j = base_job(ws, stream);
+    j.kind = gk::Kind::I8;
+    j.out = gk::Out::I32;
+    j.m = m;
+    j.k = k;
+    j.n = n;
+    j.a = Side{a, rsa, csa, 0};
+    j.b = Side{b, rsb, csb, 0};
+    j.c = c;
+    j.rsc = rsc;
+    j.csc = csc;
+    j.alpha_i = alpha;
+    j.beta_i = beta;
+    j.bias = has_bias ? bias : nullptr;
+    j.bias_axis = has_bias ? bias_dim : GK_AXIS_NONE;
+    j.act = act;
+    return execute(j);
+}
+
+int gk_gemm_i8_fused_unchecked(gk_workspace* ws, size_t m, size_t k, size_t n, int32_t alpha,
+                               const int8_t* a, ptrdiff_t rsa, ptrdiff_t csa, const int8_t* b,
+                               ptrdiff_t rsb, ptrdiff_t csb, int32_t beta, int32_t* c,
+                               ptrdiff_t rsc, ptrdiff_t csc, const int32_t* bias, int bias_dim,
+                               int has_bias, int act, gk_parallelism par, gk_stream_t stream) {
+    (void)par_ignored(par);
+    return i8_fused(ws, m, k, n, alpha, a, rsa, csa, b, rsb, csb, beta, c, rsc, csc, bias,
+                    bias_dim, has_bias, act, stream);
+}
+
+int gk_gemm_i8_fused(gk_workspace* ws, int32_t alpha, gk_matref a, gk_matref b, int32_t beta,
+                     gk_matmut c, const int32_t* bias, size_t bias_len, int bias_dim, int act,
+                     gk_parallelism par, gk_stream_t stream) {
+    int rc = validate_gemm_views(a, b, c, 1, 4);
+    if (rc) return rc;
+    if (bias) {
+        // the bias check of gemmkit's gemm_fused (gemmkit/src/api.rs:318-330)
+        const size_t want = bias_dim == GK_AXIS_COL ? b.cols : a.rows;
+        if (bias_dim != GK_AXIS_ROW && bias_dim != GK_AXIS_COL)
+            return set_err(GK_EINVAL, "gemmkit: bias dimension must be row or column");
+        if (bias_len != want)
+            return set_err(GK_EINVAL, "gemmkit: %s bias length %zu does not match %s = %zu",
+                           bias_dim == GK_AXIS_COL ? "per-column" : "per-row", bias_len,
+                           bias_dim == GK_AXIS_COL ? "n" : "m", want);
+    }
+    (void)par_ignored(par);
+    return i8_fused(ws, a.rows, a.cols, b.cols, alpha, static_cast<const int8_t*>(a.data), a.rs,
+                    a.cs, static_cast<const int8_t*>(b.data), b.rs, b.cs, beta,
+                    static_cast<int32_t*>(c.data), c.rs, c.cs, bias, bias_dim, bias != nullptr,
+                    act, stream);
 }
 
 // ---- requant ------------------------------------------------------------------------------

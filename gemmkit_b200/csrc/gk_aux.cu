@@ -191,6 +191,33 @@ int launch_fused_fill_f32(float* c, int64_t m, int64_t n, int64_t rsc, int64_t c
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
+// Fused i32 epilogue with a vanishing product (k == 0 or alpha == 0): C <- act(beta*C + bias),
+// wrapping, in the user frame (AX_M = per row i, AX_N = per column j).
+__global__ void fused_fill_i32_kernel(int32_t* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,
+                                      int32_t beta, EpiParams e) {
+    const int64_t total = m * n;
+    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t j = idx / m, i = idx - j * m;
+        int32_t* p = c + i * rsc + j * csc;
+        const uint32_t x = beta == 0 ? 0u : static_cast<uint32_t>(beta) * static_cast<uint32_t>(*p);
+        uint32_t bias = 0u;
+        if (e.bias_axis == AX_M) bias = static_cast<uint32_t>(e.bias[i]);
+        if (e.bias_axis == AX_N) bias = static_cast<uint32_t>(e.bias[j]);
+        *p = static_cast<int32_t>(fused_apply_i32(e, x, bias));
+    }
+}
+
+int launch_fused_fill_i32(int32_t* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,
+                          int32_t beta, const EpiParams& e, cudaStream_t st) {
+    if (m == 0 || n == 0) return 0;
+    int64_t blocks = (m * n + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    fused_fill_i32_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(c, m, n, rsc, csc, beta,
+                                                                         e);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
 // k == 0: every element is KRequantize::apply(0, i, j), computed with the reference's own
 // sequence in f64 (this path is not hot).
 __global__ void requant_fill_kernel(uint8_t* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,

@@ -48,10 +48,21 @@ struct EpiParams {
 
 enum FusedAct : int32_t { FACT_NONE = 0, FACT_RELU = 1, FACT_LEAKY = 2 };
 
+// Division of an unsigned n < 2^31 by a fixed d as a multiply and a shift (Granlund and
+// Montgomery's round-up method): with l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1,
+// n / d = (umulhi(n, m) + n) >> l. set_fast_div() computes m and l on the host.
+struct FastDiv {
+    uint32_t d, m, s, pad;
+};
+void set_fast_div(FastDiv* f, uint32_t d);
+
 struct GemmParams {
     int64_t Mk, Nk;
     int32_t K, batch;
     int32_t tiles_m, tiles_n, tiles_per_batch, num_tiles, num_kb, group_m;
+    // tile decode divisors: tiles per batch element, tiles per rasterisation band, band height
+    // (group_m) and the height of the last band (tiles_m % group_m, or group_m)
+    FastDiv div_tpb, div_band, div_gm, div_glast;
     int32_t a_batched, b_batched;
     // Operands held in the tiled prepacked layout (see Operand::slab) are fetched with 1-D
     // bulk copies from these bases instead of through their tensor maps (nullptr = TMA).
@@ -108,6 +119,7 @@ struct TcPlan {
     int pair;  // 1: CTA-pair kernel (256-row tiles over two SMs, cluster of 2)
     int gemv;  // 1: small-M streaming kernel (Nk <= 64; bn = its MMA N)
     int split; // small-M kernel: CTAs (one cluster) sharing each tile's K blocks, 1 = none
+    int gemv_sk;  // small-M kernel: stream-K over the (tile, K block) units of all CTAs
     int pdl;   // launch with programmatic stream serialization
     int bn, nepi, tiles_m, tiles_n, num_tiles, num_kb, grid;
     int dp_tiles, sk_maxc;
@@ -116,13 +128,17 @@ struct TcPlan {
     int64_t ctr_words;   // 32-bit words of sk_ctr
 };
 void plan_tc_gemm(const TcProblem& p, bool allow_sk, TcPlan* plan);
+// Fills the tile decode divisors of gp from its tiles_m / tiles_n / tiles_per_batch / group_m.
+void set_tile_divs(GemmParams* gp);
 // allow_pair enables the CTA-pair kernel where it applies (GEMMKIT_CUDA_PAIR knob);
 // allow_gemv the small-M streaming kernel (GEMMKIT_CUDA_GEMV knob).
+// allow_gemv_sk lets the small-M kernel split its weight stream evenly over every SM with
+// stream-K partials (the caller then provides sk_part / sk_ctr scratch, plan.sk_iters > 0).
 void plan_tc_gemm2(const TcProblem& p, bool allow_sk, bool allow_pair, bool allow_gemv,
-                   TcPlan* plan);
+                   TcPlan* plan, bool allow_gemv_sk = false);
 // The small-M streaming kernel (gk_gemv.cu): plan_gemv fills `plan` and returns true when the
 // problem qualifies (batch 1, 1 <= Nk <= 64, no tile-width override, activations not tiled).
-bool plan_gemv(const TcProblem& p, TcPlan* plan);
+bool plan_gemv(const TcProblem& p, TcPlan* plan, bool allow_sk = false);
 int launch_gemv(const TcProblem& pr, const TcPlan& plan, char* err, size_t errlen);
 struct GemmParams;
 int launch_pair(const TcProblem& pr, const TcPlan& plan, const GemmParams& gp, char* err,
@@ -156,6 +172,9 @@ int launch_scale_c_f32(float* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,
 // bias axis of `e` is in the user frame too).
 int launch_fused_fill_f32(float* c, int64_t m, int64_t n, int64_t rsc, int64_t csc, float beta,
                           const EpiParams& e, cudaStream_t s);
+// The i32 counterpart (fused i32 epilogue): C <- act(beta*C + bias), wrapping, user frame.
+int launch_fused_fill_i32(int32_t* c, int64_t m, int64_t n, int64_t rsc, int64_t csc,
+                          int32_t beta, const EpiParams& e, cudaStream_t s);
 // k == 0 requant fill: the map of a zero accumulator (user frame: i = row, j = col).
 int launch_requant_fill(void* c, int64_t m, int64_t n, int64_t rsc, int64_t csc, int64_t cbs,
                         int64_t batch, const EpiParams& e, cudaStream_t s);

@@ -45,10 +45,24 @@
 
 namespace gk {
 
+// Stream-K split of the weight stream: at most this many CTAs share one tile (the planner
+// gives every CTA at least half a tile's K blocks).
+constexpr int GEMV_SK_MAXC = 3;
+
 struct GemvParams {
     int64_t Mk, Nk;
     int32_t num_kb, tiles;
     int32_t split;           // CTAs (one cluster) per tile; 1 = whole tiles, persistent
+    // Stream-K (sk = 1): the tiles x num_kb (tile, K block) units are cut into gridDim.x equal
+    // contiguous runs, one per CTA. A tile shared by several CTAs leaves one 32-bit partial
+    // accumulator tile per CTA in `part` (slot = CTA - first CTA of the tile); the last CTA to
+    // finish a 32-row quarter of it (counted in ctr, tagged with `epoch`) sums the slots in
+    // slot order and runs the epilogue.
+    int32_t sk;
+    int64_t units;
+    uint32_t* part;
+    uint32_t* ctr;
+    uint32_t epoch;
     int32_t early_weights;   // fetch the first ring of weights before griddep_wait
     const uint8_t* w_tiled;  // tiled prepacked weights, or nullptr: load through the tensor map
     int64_t w_slab;          // bytes between consecutive K blocks of w_tiled
@@ -74,35 +88,104 @@ struct GemvCfg {
     static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
     static constexpr int SLOT_BYTES = BM * NB * 4;  // one CTA's partial accumulator tile
     static constexpr int MAX_SPLIT_RING = RING_BYTES / SLOT_BYTES + 1;
-    static constexpr int TMEM_COLS = 2 * NB < 32 ? 32 : 2 * NB;
+    // Accumulators in TMEM: four, so that the epilogue of a stream-K piece (its partial store,
+    // fence and counter) never holds back the MMAs of the next items.
+    static constexpr int NACC = 4;
+    static constexpr int TMEM_COLS = NACC * NB < 32 ? 32 : NACC * NB;
     static constexpr int THREADS = 192;  // producer, MMA, 4 epilogue warps
     static constexpr int SMEM = 1024 + RING_BYTES + BAR_BYTES + CP_BYTES;
     static constexpr int CH = NB == 16 ? 16 : 32;  // TMEM columns per load
     static constexpr int NCH = NB / CH;
     static_assert(SMEM <= SMEM_LIMIT, "gemv stages exceed shared memory");
     static_assert((STAGE_BYTES % 1024) == 0, "stages must keep the 1024-byte swizzle alignment");
+    static_assert((2 * STAGES + 2 * NACC + 1) * 8 + 8 <= BAR_BYTES, "barrier area");
 };
 
-// The CTA's work items, identical for every role: whole tiles blockIdx.x, + gridDim.x, ... when
-// split == 1; else K blocks [r*num_kb/split, (r+1)*num_kb/split) of tile blockIdx.x / split,
-// r = blockIdx.x % split (the CTA's rank in its cluster).
-__device__ __forceinline__ bool gemv_next(const GemvParams& p, int& it, int& tile, int& k0,
-                                          int& k1) {
-    if (p.split > 1) {
-        if (it > 0) return false;
-        tile = static_cast<int>(blockIdx.x) / p.split;
-        const int r = static_cast<int>(blockIdx.x) - tile * p.split;
-        k0 = static_cast<int>(static_cast<int64_t>(r) * p.num_kb / p.split);
-        k1 = static_cast<int>(static_cast<int64_t>(r + 1) * p.num_kb / p.split);
-    } else {
-        tile = static_cast<int>(blockIdx.x) + it * static_cast<int>(gridDim.x);
-        if (tile >= p.tiles) return false;
-        k0 = 0;
-        k1 = p.num_kb;
+// One work item of a CTA: K blocks [k0, k1) of `tile`; nctr > 1 marks a tile shared with
+// other CTAs (stream-K), of which this CTA holds partial slot `slot`.
+struct GemvItem {
+    int tile, k0, k1, slot, nctr;
+};
+
+// The CTA's work items, identical for every role.
+//  * split > 1: K blocks [r*num_kb/split, (r+1)*num_kb/split) of tile blockIdx.x / split,
+//    r = blockIdx.x % split (the CTA's rank in its cluster);
+//  * sk: the CTA's run [s, e) of units; first the pieces of the (at most two) tiles it shares
+//    with its neighbours, then the tiles it covers whole, so that every shared tile is
+//    finished early by all of its CTAs and its reduction overlaps the rest of the streaming;
+//  * otherwise whole tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+struct GemvSched {
+    int nsh, w_lo, w_cnt;
+    GemvItem sh0, sh1;  // the shared pieces (two members, not an array: no local memory)
+
+    __device__ __forceinline__ static int64_t start(const GemvParams& p, int c) {
+        return static_cast<int64_t>(c) * p.units / static_cast<int64_t>(gridDim.x);
     }
-    ++it;
-    return true;
-}
+    // the CTA whose run holds unit T: the largest c with start(c) <= T
+    __device__ __forceinline__ static int owner(const GemvParams& p, int64_t T) {
+        const int64_t G = gridDim.x;
+        const int64_t c = ((T + 1) * G + p.units - 1) / p.units - 1;
+        return static_cast<int>(c < 0 ? 0 : (c >= G ? G - 1 : c));
+    }
+    __device__ __forceinline__ void shared_piece(const GemvParams& p, int tile, int k0, int k1) {
+        const int64_t t0 = static_cast<int64_t>(tile) * p.num_kb;
+        const int cf = owner(p, t0), cl = owner(p, t0 + p.num_kb - 1);
+        const GemvItem it{tile, k0, k1, static_cast<int>(blockIdx.x) - cf, cl - cf + 1};
+        if (nsh == 0)
+            sh0 = it;
+        else
+            sh1 = it;
+        ++nsh;
+    }
+    __device__ __forceinline__ explicit GemvSched(const GemvParams& p) {
+        nsh = 0;
+        w_lo = 0;
+        w_cnt = 0;
+        sh0 = sh1 = GemvItem{0, 0, 0, 0, 1};
+        if (!p.sk) return;
+        const int nkb = p.num_kb;
+        const int64_t s = start(p, blockIdx.x), e = start(p, blockIdx.x + 1);
+        if (e <= s) return;
+        const int tA = static_cast<int>(s / nkb), tB = static_cast<int>((e - 1) / nkb);
+        const int sA = static_cast<int>(s - static_cast<int64_t>(tA) * nkb);
+        const int64_t eA = e - static_cast<int64_t>(tA) * nkb;
+        if (sA != 0) shared_piece(p, tA, sA, eA < nkb ? static_cast<int>(eA) : nkb);
+        const int eB = static_cast<int>(e - static_cast<int64_t>(tB) * nkb);
+        if (eB != nkb && !(tB == tA && sA != 0)) {
+            const int64_t sB = s - static_cast<int64_t>(tB) * nkb;
+            shared_piece(p, tB, sB > 0 ? static_cast<int>(sB) : 0, eB);
+        }
+        w_lo = static_cast<int>((s + nkb - 1) / nkb);
+        const int w_hi = static_cast<int>(e / nkb) - 1;
+        w_cnt = w_hi >= w_lo ? w_hi - w_lo + 1 : 0;
+    }
+    __device__ __forceinline__ bool get(const GemvParams& p, int idx, GemvItem& it) const {
+        if (p.sk) {
+            if (idx < nsh) {
+                it = idx == 0 ? sh0 : sh1;
+                return true;
+            }
+            if (idx - nsh < w_cnt) {
+                it = GemvItem{w_lo + idx - nsh, 0, p.num_kb, 0, 1};
+                return true;
+            }
+            return false;
+        }
+        if (p.split > 1) {
+            if (idx > 0) return false;
+            const int tile = static_cast<int>(blockIdx.x) / p.split;
+            const int r = static_cast<int>(blockIdx.x) - tile * p.split;
+            it = GemvItem{tile, static_cast<int>(static_cast<int64_t>(r) * p.num_kb / p.split),
+                          static_cast<int>(static_cast<int64_t>(r + 1) * p.num_kb / p.split), 0,
+                          1};
+            return true;
+        }
+        const int tile = static_cast<int>(blockIdx.x) + idx * static_cast<int>(gridDim.x);
+        if (tile >= p.tiles) return false;
+        it = GemvItem{tile, 0, p.num_kb, 0, 1};
+        return true;
+    }
+};
 
 __device__ __forceinline__ void epi_bar_sync() {
     asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -128,9 +211,9 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
     uint64_t* tfull = bars + 2 * STAGES;
-    uint64_t* tempty = tfull + 2;
-    uint64_t* drain = tfull + 4;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 5);
+    uint64_t* tempty = tfull + C::NACC;
+    uint64_t* drain = tfull + 2 * C::NACC;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     ColParam* cp = reinterpret_cast<ColParam*>(smem + C::RING_BYTES + C::BAR_BYTES);
     uint32_t* cbias = reinterpret_cast<uint32_t*>(cp + NB);
@@ -144,7 +227,7 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int a = 0; a < 2; ++a) {
+        for (int a = 0; a < C::NACC; ++a) {
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
         }
@@ -187,22 +270,23 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
                     tma_load_3d(dw, &tmW, &full[stage], kb * BKE, tile * BM, 0);
             };
             // The first ring of weight blocks, ahead of the grid dependency (prepacked only).
+            const GemvSched sch(p);
+            GemvItem wi;
             int pre = 0;
             if (p.early_weights && p.w_tiled) {
-                int it = 0, tile, k0, k1;
-                while (pre < STAGES && gemv_next(p, it, tile, k0, k1))
-                    for (int kb = k0; kb < k1 && pre < STAGES; ++kb, ++pre) {
+                for (int n = 0; pre < STAGES && sch.get(p, n, wi); ++n)
+                    for (int kb = wi.k0; kb < wi.k1 && pre < STAGES; ++kb, ++pre) {
                         mbar_arrive_expect_tx(&full[pre], C::STAGE_BYTES);
-                        issue_w(pre, tile, kb);
+                        issue_w(pre, wi.tile, kb);
                     }
             }
             griddep_wait();
-            int it = 0, tile, k0, k1;
             int stage = 0, idx = 0;
             uint32_t phase = 0, issued = 0, last_par = 0;
             bool ok = true;
-            while (ok && gemv_next(p, it, tile, k0, k1)) {
-                for (int kb = k0; kb < k1; ++kb, ++idx) {
+            for (int n = 0; ok && sch.get(p, n, wi); ++n) {
+                const int tile = wi.tile;
+                for (int kb = wi.k0; kb < wi.k1; ++kb, ++idx) {
                     if (idx >= pre) {
                         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status,
                                        GK_DEV_TIMEOUT_PRODUCER, tmo)) {
@@ -242,13 +326,15 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
                 idesc = idesc_i8(BM, NB);
             else
                 idesc = idesc_f16(BM, NB, KIND == Kind::BF16);
-            int it = 0, tile, k0, k1;
+            const GemvSched sch(p);
+            GemvItem wi;
             int stage = 0, local = 0;
             uint32_t phase = 0;
             bool ok = true;
-            while (ok && gemv_next(p, it, tile, k0, k1)) {
-                const int acc = local & 1;
-                const uint32_t aph = (local >> 1) & 1u;
+            for (int n = 0; ok && sch.get(p, n, wi); ++n) {
+                const int k0 = wi.k0, k1 = wi.k1;
+                const int acc = local % C::NACC;
+                const uint32_t aph = (local / C::NACC) & 1u;
                 ++local;
                 if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, p.status, GK_DEV_TIMEOUT_MMA,
                                tmo)) {
@@ -310,17 +396,21 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
             epi_bar_sync();
         }
 
-        int it = 0, tile, k0, k1;
+        const GemvSched sch(p);
+        GemvItem wi;
         int local = 0;
-        while (gemv_next(p, it, tile, k0, k1)) {
-            const int acc = local & 1;
-            const uint32_t aph = (local >> 1) & 1u;
+        for (int n = 0; sch.get(p, n, wi); ++n) {
+            const int tile = wi.tile;
+            const int acc = local % C::NACC;
+            const uint32_t aph = (local / C::NACC) & 1u;
             ++local;
             grow = static_cast<int64_t>(tile) * BM + row;
             const bool row_ok = grow < p.Mk;
             // this row's requant constants, fetched while the MMAs run
             if constexpr (OUT == Out::F32)
                 r_fb = (e.fbias_axis == AX_M && row_ok) ? e.fbias[grow] : 0.0f;
+            if constexpr (OUT == Out::I32)  // the fused i32 epilogue's per-row bias
+                r_bp = (e.bias_axis == AX_M && row_ok) ? static_cast<uint32_t>(e.bias[grow]) : 0u;
             if constexpr (QUANT) {
                 float rs = e.scale;
                 int32_t rb = 0;
@@ -348,6 +438,64 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
             if (lane == 0) mbar_arrive(&tempty[acc]);
             have = true;
             if (p.split > 1) break;  // one item; summed across the cluster below
+            if (wi.nctr > 1) {
+                // A shared tile: publish this CTA's partial rows in its slot, then count this
+                // warp's 32-row quarter; the last of the tile's CTAs to arrive sums the slots
+                // in slot order (exact for integers, a fixed order for floats) and finishes.
+                uint32_t* base = p.part + static_cast<int64_t>(tile) * GEMV_SK_MAXC * (BM * NB) +
+                                 static_cast<int64_t>(row) * NB;
+                uint32_t* mine = base + static_cast<int64_t>(wi.slot) * (BM * NB);
+#pragma unroll
+                for (int c = 0; c < NCH; ++c)
+#pragma unroll
+                    for (int g = 0; g < CH / 4; ++g)
+                        st_global_v4(mine + c * CH + 4 * g, v[c][4 * g], v[c][4 * g + 1],
+                                     v[c][4 * g + 2], v[c][4 * g + 3]);
+                __threadfence();
+                __syncwarp();
+                uint32_t last = 0;
+                if (lane == 0) {
+                    uint32_t* ctr = p.ctr + static_cast<int64_t>(tile) * 4 + q;
+                    uint32_t old = atomicAdd(ctr, 0u);
+                    while (true) {
+                        const uint32_t nv =
+                            (old >> 8) == p.epoch ? old + 1u : ((p.epoch << 8) | 1u);
+                        const uint32_t prev = atomicCAS(ctr, old, nv);
+                        if (prev == old) {
+                            last = (nv & 0xFFu) == static_cast<uint32_t>(wi.nctr) ? 1u : 0u;
+                            break;
+                        }
+                        old = prev;
+                    }
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (!last) continue;
+                __threadfence();
+#pragma unroll
+                for (int c = 0; c < NCH; ++c)
+#pragma unroll
+                    for (int i = 0; i < CH; ++i) v[c][i] = 0u;
+                for (int j = 0; j < wi.nctr; ++j) {
+                    const uint4* src = reinterpret_cast<const uint4*>(
+                        base + static_cast<int64_t>(j) * (BM * NB));
+#pragma unroll
+                    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+                        for (int g = 0; g < CH / 4; ++g) {
+                            const uint4 x = __ldcg(src + (c * CH) / 4 + g);
+                            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) {
+                                uint32_t& d = v[c][4 * g + t];
+                                if constexpr (KIND == Kind::I8)
+                                    d += xs[t];
+                                else
+                                    d = __float_as_uint(__fadd_rn(__uint_as_float(d),
+                                                                  __uint_as_float(xs[t])));
+                            }
+                        }
+                }
+            }
             int qm = QM_GENERAL;
             if constexpr (QUANT) qm = pick_quant_mode(e, r_se);
             with_quant_mode<QUANT>(qm, [&](auto qm_tag) {
@@ -493,8 +641,21 @@ static int launch_gemv_nb(const TcProblem& pr, const TcPlan& plan, GemvParams gp
     }
     if (split < 1) split = 1;
     gp.split = split;
-    const int grid = split > 1 ? plan.tiles_m * split
-                               : (plan.tiles_m < sm_count() ? plan.tiles_m : sm_count());
+    int grid = split > 1 ? plan.tiles_m * split
+                         : (plan.tiles_m < sm_count() ? plan.tiles_m : sm_count());
+    if (plan.gemv_sk) {
+        if (!pr.sk_part || !pr.sk_ctr) {
+            snprintf(err, errlen, "gemmkit: internal error: small-M stream-K without scratch");
+            return 1;
+        }
+        gp.sk = 1;
+        gp.split = 1;
+        gp.units = plan.sk_iters;
+        gp.part = pr.sk_part;
+        gp.ctr = pr.sk_ctr;
+        gp.epoch = pr.sk_epoch;
+        grid = plan.grid;
+    }
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
@@ -542,7 +703,7 @@ static int dispatch_gemv(const TcProblem& pr, const TcPlan& plan, const GemvPara
     }
 }
 
-bool plan_gemv(const TcProblem& p, TcPlan* plan) {
+bool plan_gemv(const TcProblem& p, TcPlan* plan, bool allow_sk) {
     // the activation side comes through a tensor map; a tiled operand there (a prepacked
     // right-hand side with <= 64 columns) stays with the general kernel
     if (p.batch != 1 || p.Nk > 64 || p.Nk < 1 || p.bn != 0 || p.b.slab != 0) return false;
@@ -569,6 +730,20 @@ bool plan_gemv(const TcProblem& p, TcPlan* plan) {
     }
     pl.split = split;
     pl.grid = split > 1 ? pl.tiles_m * split : (pl.tiles_m < sms ? pl.tiles_m : sms);
+    // Stream-K over the weight stream when whole tiles would leave SMs idle or unevenly loaded
+    // (tiles not a multiple of the SM count) and every SM still gets at least half a tile of
+    // K blocks (so at most GEMV_SK_MAXC CTAs share a tile): the bytes each SM streams, which
+    // bound a call, are then the same on every SM.
+    const int64_t units = static_cast<int64_t>(pl.tiles_m) * pl.num_kb;
+    if (allow_sk && split == 1 && pl.num_kb >= 2 && pl.tiles_m % sms != 0 &&
+        units / sms >= (pl.num_kb + 1) / 2) {
+        pl.gemv_sk = 1;
+        pl.grid = sms;
+        pl.sk_iters = units;
+        pl.sk_maxc = GEMV_SK_MAXC;
+        pl.ctr_words = static_cast<int64_t>(pl.tiles_m) * 4;
+        pl.part_words = static_cast<int64_t>(pl.tiles_m) * GEMV_SK_MAXC * BM * pl.bn;
+    }
     pl.dp_tiles = pl.num_tiles;
     *plan = pl;
     return true;

@@ -28,16 +28,24 @@ struct alignas(16) ColParam {
     uint32_t pad;
 };
 
-__device__ __forceinline__ void make_scale_param(float s, double& se, double& nms, uint32_t& ulo,
-                                                 uint32_t& uhi) {
+// The two parts of a scale's constants: se / nms (every requantize path), and the
+// accumulator clamp (only the general path; it costs an f64 division).
+__device__ __forceinline__ void make_scale_se(float s, double& se, double& nms) {
     const double s64 = static_cast<double>(s);
     se = s64 < 2048.0 ? s64 : 2048.0;
     nms = -(4503601774854144.0 * se);
+}
+__device__ __forceinline__ void make_scale_clamp(double se, uint32_t& ulo, uint32_t& uhi) {
     const double vs = ceil(2048.0 / se) + 1.0;
     const int vhi = vs >= 2147483647.0 ? 2147483647 : static_cast<int>(vs);
     const int vlo = vhi == 2147483647 ? (-2147483647 - 1) : -vhi - 1;
     ulo = static_cast<uint32_t>(vlo) + 0x80000000u;
     uhi = static_cast<uint32_t>(vhi) + 0x80000000u;
+}
+__device__ __forceinline__ void make_scale_param(float s, double& se, double& nms, uint32_t& ulo,
+                                                 uint32_t& uhi) {
+    make_scale_se(s, se, nms);
+    make_scale_clamp(se, ulo, uhi);
 }
 
 // zp + rne(fl64(f64(v) * f64(scale))) for v = acc +wrap bias, exactly (the caller clamps to
@@ -66,12 +74,21 @@ __device__ __forceinline__ int requant_q(uint32_t acc, uint32_t bias_plus, doubl
 // exact when the scale is at most 2^-9 and zp is even: |v| <= 2^31 then bounds |p| by 2^22, so
 // the rounded integer plus zp sits in the low word, and a tie of p + zp goes to the even
 // neighbour of p shifted by the even zp, the same integer as rne(p) + zp.
+// (Written as one PTX sequence: the 64-bit operand is assembled from the sum and the
+// exponent word in place, which keeps the per-element instruction count at its minimum.)
 __device__ __forceinline__ int requant_q_small(uint32_t acc, uint32_t bias_plus, double se,
                                                double nms, double magic) {
-    const uint32_t u = acc + bias_plus;
-    const double d = __hiloint2double(0x43300000, static_cast<int>(u));
-    const double p = __fma_rn(d, se, nms);
-    return __double2loint(__dadd_rn(p, magic));
+    int q;
+    asm("{\n\t.reg .b32 u, h;\n\t.reg .f64 d, p;\n\t"
+        "add.u32 u, %1, %2;\n\t"
+        "mov.b32 h, 0x43300000;\n\t"
+        "mov.b64 d, {u, h};\n\t"
+        "fma.rn.f64 p, d, %3, %4;\n\t"
+        "add.rn.f64 p, p, %5;\n\t"
+        "mov.b64 {%0, h}, p;\n\t}"
+        : "=r"(q)
+        : "r"(acc), "r"(bias_plus), "d"(se), "d"(nms), "d"(magic));
+    return q;
 }
 
 // Four values saturated to the output band and packed little-endian (x0 in the low byte).
@@ -88,17 +105,28 @@ __device__ __forceinline__ uint32_t pack4_sat(int x0, int x1, int x2, int x3) {
     return d;
 }
 
+__device__ __forceinline__ uint32_t fast_div(const FastDiv& f, uint32_t n) {
+    return (__umulhi(n, f.m) + n) >> f.s;
+}
+
+// Tile t -> (batch element b, tile row tm, tile column tn): batch-major, then bands of group_m
+// tile rows, column by column inside a band (so a wave of CTAs shares A rows and B columns in
+// L2). Divisions by the fixed divisors of the launch use their multiply-shift forms.
 __device__ __forceinline__ void decode_tile(int t, const GemmParams& p, int& b, int& tm,
                                             int& tn) {
-    b = t / p.tiles_per_batch;
-    const int r = t - b * p.tiles_per_batch;
-    const int band_tiles = p.group_m * p.tiles_n;
-    const int band = r / band_tiles;
-    const int first_m = band * p.group_m;
-    const int gsize = min(p.tiles_m - first_m, p.group_m);
-    const int rr = r - band * band_tiles;
-    tm = first_m + rr % gsize;
-    tn = rr / gsize;
+    const uint32_t ut = static_cast<uint32_t>(t);
+    const uint32_t ub = fast_div(p.div_tpb, ut);
+    const uint32_t r = ut - ub * p.div_tpb.d;
+    const uint32_t band = fast_div(p.div_band, r);
+    const uint32_t first_m = band * static_cast<uint32_t>(p.group_m);
+    const uint32_t rr = r - band * p.div_band.d;
+    const FastDiv& g =
+        static_cast<uint32_t>(p.tiles_m) - first_m < static_cast<uint32_t>(p.group_m) ? p.div_glast
+                                                                                    : p.div_gm;
+    const uint32_t q = fast_div(g, rr);
+    b = static_cast<int>(ub);
+    tn = static_cast<int>(q);
+    tm = static_cast<int>(first_m + (rr - q * g.d));
 }
 
 // One unit of a CTA's work: K blocks [k0, k1) of `tile`. nctr > 1 marks a stream-K tile cut
@@ -172,6 +200,17 @@ __device__ __forceinline__ float fused_apply(const EpiParams& e, float v, float 
     return v;
 }
 
+// The integer counterpart of fused_apply for i32 outputs (an extension: gemmkit's FusedEpi is
+// float-only, gemmkit/src/kernel/epilogue.rs:258-330): after alpha*acc + beta*C (wrapping, as
+// int32_epilogue, gemmkit/src/kernel/int.rs:36-120) add the bias with wrap-around, then ReLU
+// as max(v, 0) on the signed value. Only the i32 entry with a fused epilogue sets
+// e.bias / e.act for an i32 output.
+__device__ __forceinline__ uint32_t fused_apply_i32(const EpiParams& e, uint32_t v, uint32_t bias) {
+    if (e.bias_axis != AX_NONE) v += bias;
+    if (e.act == FACT_RELU) v = static_cast<uint32_t>(max(static_cast<int32_t>(v), 0));
+    return v;
+}
+
 // Output stores: the local C and every mirror (same byte offset).
 __device__ __forceinline__ void out_v4(const EpiParams& e, int64_t byte_off, uint32_t a,
                                        uint32_t b, uint32_t c, uint32_t d) {
@@ -215,7 +254,9 @@ __device__ __forceinline__ void with_quant_mode(int qm, F&& f) {
 }
 
 // The epilogue of one chunk of CH accumulator columns held by this thread (its row), starting
-// at column gc of the output; columns at or past Nk are not written.
+// at column gc of the output; columns at or past Nk are not written. For quantized outputs cp
+// holds the chunk's per-column ColParams (per-column scale) and cb the chunk's per-column
+// bias + 2^31 (per-column bias), both in shared memory; r_* are this row's values.
 template <Out OUT, int CH, int QM = QM_GENERAL>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t Nk,
                                                const EpiParams& e, int64_t obase, int64_t gc,
@@ -273,7 +314,7 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t 
         } else if (e.bias_axis == AX_N) {
 #pragma unroll
             for (int i = 0; i < CH; ++i)
-                q[i] = requant_q(v[i], cp[i].bias_plus, r_se, r_nms, r_ulo, r_uhi, e.zp);
+                q[i] = requant_q(v[i], cb[i], r_se, r_nms, r_ulo, r_uhi, e.zp);
         } else {
 #pragma unroll
             for (int i = 0; i < CH; ++i)
@@ -299,10 +340,14 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t 
                                    static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3))));
         }
     } else if constexpr (OUT == Out::I32) {
+        // r_bp carries this row's i32 bias (fused i32 epilogue with a per-row bias); a
+        // per-column bias is read from e.bias (the fused i32 entry is not batched)
         int32_t* out = static_cast<int32_t*>(e.out);
         uint32_t r[CH];
         const uint32_t al = static_cast<uint32_t>(e.alpha_i);
         const uint32_t be = static_cast<uint32_t>(e.beta_i);
+        const bool fused = e.bias_axis != AX_NONE || e.act != FACT_NONE;
+        const bool colb = e.bias_axis == AX_N;
         if (e.vec && full_chunk) {
             int32_t* dst = out + obase + gc;
             if (be != 0u) {
@@ -318,6 +363,13 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t 
 #pragma unroll
                 for (int i = 0; i < CH; ++i) r[i] = al * v[i];
             }
+            if (fused) {
+#pragma unroll
+                for (int i = 0; i < CH; ++i)
+                    r[i] = fused_apply_i32(e, r[i],
+                                           colb ? static_cast<uint32_t>(__ldg(e.bias + gc + i))
+                                                : r_bp);
+            }
 #pragma unroll
             for (int g = 0; g < CH / 4; ++g)
                 out_v4(e, (obase + gc + g * 4) * 4, r[g * 4], r[g * 4 + 1], r[g * 4 + 2],
@@ -329,6 +381,9 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[32], int64_t 
                 const int64_t off = obase + (gc + i) * e.cso;
                 uint32_t o = al * v[i];
                 if (be != 0u) o += be * static_cast<uint32_t>(out[off]);
+                if (fused)
+                    o = fused_apply_i32(e, o,
+                                        colb ? static_cast<uint32_t>(__ldg(e.bias + gc + i)) : r_bp);
                 out_1<int32_t>(e, off, static_cast<int32_t>(o));
             }
         }

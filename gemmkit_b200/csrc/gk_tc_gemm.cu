@@ -306,6 +306,8 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
             const ColParam* cp = cparams + acc * BN;
             const float r_fb = (OUT == Out::F32 && e.fbias_axis == AX_M && row_ok)
                                    ? e.fbias[grow] : 0.0f;
+            if constexpr (OUT == Out::I32)  // the fused i32 epilogue's per-row bias
+                r_bp = (e.bias_axis == AX_M && row_ok) ? static_cast<uint32_t>(e.bias[grow]) : 0u;
 
             if (col_params && !warp_wait(&pready[acc], aph, abort_flag, p.status,
                                          GK_DEV_TIMEOUT_EPILOGUE, tmo))
@@ -455,6 +457,26 @@ static PFN_tmapEncodeTiled get_encode() {
             fn = reinterpret_cast<PFN_tmapEncodeTiled>(f);
     });
     return fn;
+}
+
+void set_fast_div(FastDiv* f, uint32_t d) {
+    if (d == 0) d = 1;
+    uint32_t l = 0;
+    while (l < 31 && (1u << l) < d) ++l;
+    f->d = d;
+    f->s = l;
+    f->m = static_cast<uint32_t>(((static_cast<uint64_t>(1) << 32) *
+                                  ((static_cast<uint64_t>(1) << l) - d)) / d + 1);
+    f->pad = 0;
+}
+
+void set_tile_divs(GemmParams* gp) {
+    const uint32_t gm = gp->group_m > 0 ? static_cast<uint32_t>(gp->group_m) : 1u;
+    const uint32_t tm = gp->tiles_m > 0 ? static_cast<uint32_t>(gp->tiles_m) : 1u;
+    set_fast_div(&gp->div_tpb, static_cast<uint32_t>(gp->tiles_per_batch));
+    set_fast_div(&gp->div_band, gm * static_cast<uint32_t>(gp->tiles_n));
+    set_fast_div(&gp->div_gm, gm);
+    set_fast_div(&gp->div_glast, tm % gm ? tm % gm : gm);
 }
 
 static __device__ unsigned int g_status[64];
@@ -622,6 +644,7 @@ static int launch_one(const TcProblem& pr, const TcPlan& plan, GemmParams gp, ch
     }
     gp.tiles_n = plan.tiles_n;
     gp.tiles_per_batch = gp.tiles_m * gp.tiles_n;
+    set_tile_divs(&gp);
     gp.num_tiles = plan.num_tiles;
     gp.dp_tiles = plan.dp_tiles;
     gp.sk_iters = plan.sk_iters;
@@ -708,8 +731,8 @@ void plan_tc_gemm(const TcProblem& p, bool allow_sk, TcPlan* plan) {
 }
 
 void plan_tc_gemm2(const TcProblem& p, bool allow_sk, bool allow_pair, bool allow_gemv,
-                   TcPlan* plan) {
-    if (allow_gemv && plan_gemv(p, plan)) return;
+                   TcPlan* plan, bool allow_gemv_sk) {
+    if (allow_gemv && plan_gemv(p, plan, allow_gemv_sk)) return;
     plan_tc_gemm(p, allow_sk, plan);
     TcPlan& pl = *plan;
     if (!allow_pair || pl.bn != 256 || p.Mk < 2 * BM) return;

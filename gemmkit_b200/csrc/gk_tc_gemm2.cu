@@ -274,51 +274,79 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
             mbar_wait(drain, 0, &dummy, p.status, GK_DEV_TIMEOUT_DRAIN, tmo);
         }
     } else {
-        // ---------------- epilogue (warps 2 .. 9, both CTAs) ----------------
+        // ---------------- epilogue (warps 2 .. 1 + NEPI, both CTAs) ----------------
         const int q = warp & 3;
         const int cgroup = (warp - 2) >> 2;  // which column group of the item this warp drains
         const int et = threadIdx.x - 64;
         const EpiParams& e = p.e;
         const int row = q * 32 + lane;
-        const bool col_params = C::QUANT && (e.scale_axis == AX_N || e.bias_axis == AX_N);
+        // A per-column scale becomes ColParams once per item for the whole CTA (shared memory,
+        // the pready barrier). With a per-row or per-tensor scale the only per-column value is
+        // the bias, which each warp fetches for its own columns into a private shared-memory
+        // slice, so the epilogue warps never wait for one another.
+        const bool col_params = C::QUANT && e.scale_axis == AX_N;
+        const bool warp_bias = C::QUANT && !col_params && e.bias_axis == AX_N;
+        uint32_t* wslice = reinterpret_cast<uint32_t*>(cparams) + (warp - 2) * C::WCOLS;
+        constexpr int WB = C::WCOLS / 32;  // bias values a lane fetches for its warp's slice
+        // The 16-warp form (short K: the epilogue is the kernel) fetches the next item's slice
+        // into registers ahead of time; the 8-warp form (long K: the epilogue hides behind the
+        // mainloop) loads it when the slice is written, leaving its registers to the chunks.
+        constexpr int WBR = EPI16 ? WB : 1;
 
+        struct Pos {
+            int b, tm, tn, c0, width;
+        };
+        auto locate = [&](int t) {
+            Pos ps;
+            int tile;
+            pair_item<BN>(t, p, tile, ps.c0, ps.width);
+            decode_tile(tile, p, ps.b, ps.tm, ps.tn);
+            return ps;
+        };
         struct Raw {
             float rscale, cscale;
             int32_t rbias, cbias;
+            int32_t wb[WBR];
         };
-        auto load_raw = [&](int t, Raw& r) {
-            int tile, c0, width;
-            pair_item<BN>(t, p, tile, c0, width);
-            int b, tm, tn;
-            decode_tile(tile, p, b, tm, tn);
-            const int64_t grow = static_cast<int64_t>(tm) * 2 * BM + rank * BM + row;
-            const int64_t gc = static_cast<int64_t>(tn) * BN + c0 + et;
-            const bool rok = grow < p.Mk, cok = et < width && gc < p.Nk;
+        // bias j of this lane's share of the warp's slice for the item at ps
+        auto slice_bias = [&](const Pos& ps, int j) {
+            const int wcols = ps.width / C::NGROUPS;
+            const int64_t gc0 = static_cast<int64_t>(ps.tn) * BN + ps.c0 + cgroup * wcols;
+            const int cj = lane + 32 * j;
+            return (cj < wcols && gc0 + cj < p.Nk) ? e.bias[ps.b * e.bias_bs + gc0 + cj] : 0;
+        };
+        auto load_raw = [&](const Pos& ps, Raw& r) {
+            const int64_t grow = static_cast<int64_t>(ps.tm) * 2 * BM + rank * BM + row;
+            const bool rok = grow < p.Mk;
             r.rscale = e.scale;
             r.cscale = 1.0f;
             r.rbias = 0;
             r.cbias = 0;
-            if (e.scale_axis == AX_M && rok) r.rscale = e.scales[b * e.scale_bs + grow];
-            if (e.bias_axis == AX_M && rok) r.rbias = e.bias[b * e.bias_bs + grow];
-            if (e.scale_axis == AX_N && cok) r.cscale = e.scales[b * e.scale_bs + gc];
-            if (e.bias_axis == AX_N && cok) r.cbias = e.bias[b * e.bias_bs + gc];
+            if (e.scale_axis == AX_M && rok) r.rscale = e.scales[ps.b * e.scale_bs + grow];
+            if (e.bias_axis == AX_M && rok) r.rbias = e.bias[ps.b * e.bias_bs + grow];
+            if (col_params) {
+                const int64_t gc = static_cast<int64_t>(ps.tn) * BN + ps.c0 + et;
+                const bool cok = et < ps.width && gc < p.Nk;
+                if (cok) r.cscale = e.scales[ps.b * e.scale_bs + gc];
+                if (e.bias_axis == AX_N && cok) r.cbias = e.bias[ps.b * e.bias_bs + gc];
+            }
+            if constexpr (EPI16) {
+                if (warp_bias) {
+#pragma unroll
+                    for (int j = 0; j < WB; ++j) r.wb[j] = slice_bias(ps, j);
+                }
+            }
         };
         double r_se = 0.0, r_nms = 0.0;
         uint32_t r_ulo = 0, r_uhi = 0, r_bp = 0x80000000u;
-        auto commit = [&](const Raw& r, int buf) {
-            if (e.scale_axis != AX_N) make_scale_param(r.rscale, r_se, r_nms, r_ulo, r_uhi);
+        auto commit = [&](const Raw& r, const Pos& ps, int buf) {
+            // the clamp of a per-row scale is computed only if the general path runs
+            if (e.scale_axis != AX_N) make_scale_se(r.rscale, r_se, r_nms);
             r_bp = static_cast<uint32_t>(r.rbias) + 0x80000000u;
             if (col_params) {
                 if (et < BN) {
                     ColParam c;
-                    if (e.scale_axis == AX_N) {
-                        make_scale_param(r.cscale, c.se, c.nms, c.ulo, c.uhi);
-                    } else {
-                        c.se = 0.0;
-                        c.nms = 0.0;
-                        c.ulo = 0;
-                        c.uhi = 0;
-                    }
+                    make_scale_param(r.cscale, c.se, c.nms, c.ulo, c.uhi);
                     c.bias_plus = static_cast<uint32_t>(r.cbias) + 0x80000000u;
                     c.pad = 0;
                     cparams[buf * BN + et] = c;
@@ -326,20 +354,31 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
                 }
                 mbar_arrive(&pready[buf]);
             }
+            if (warp_bias) {
+                __syncwarp();  // every lane is done with the previous item's slice
+#pragma unroll
+                for (int j = 0; j < WB; ++j) {
+                    int32_t v;
+                    if constexpr (EPI16)
+                        v = r.wb[j];
+                    else
+                        v = slice_bias(ps, j);
+                    wslice[lane + 32 * j] = static_cast<uint32_t>(v) + 0x80000000u;
+                }
+                __syncwarp();
+            }
         };
 
         griddep_wait();  // parameters and outputs may belong to the previous kernel
         Raw raw;
+        Pos pos = locate(pair);
         if (C::QUANT && pair < n_items) {
-            load_raw(pair, raw);
-            commit(raw, 0);
+            load_raw(pos, raw);
+            commit(raw, pos, 0);
         }
         int local = 0;
         for (int t = pair; t < n_items; t += npairs, ++local) {
-            int tile, c0, width;
-            pair_item<BN>(t, p, tile, c0, width);
-            int b, tm, tn;
-            decode_tile(tile, p, b, tm, tn);
+            const int b = pos.b, tm = pos.tm, tn = pos.tn, c0 = pos.c0, width = pos.width;
             const int acc = local & 1;
             const uint32_t aph = (local >> 1) & 1;
             const int64_t grow = static_cast<int64_t>(tm) * 2 * BM + rank * BM + row;
@@ -348,9 +387,12 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
             const ColParam* cp = cparams + acc * BN;
             const float r_fb = (OUT == Out::F32 && e.fbias_axis == AX_M && row_ok)
                                    ? e.fbias[grow] : 0.0f;
+            if constexpr (OUT == Out::I32)  // the fused i32 epilogue's per-row bias
+                r_bp = (e.bias_axis == AX_M && row_ok) ? static_cast<uint32_t>(e.bias[grow]) : 0u;
             const int wcols = width / C::NGROUPS;  // columns per warp group
             const int col_base = cgroup * wcols;
             const int nch = wcols / CH;
+            const uint32_t* cb = warp_bias ? wslice : cbias + acc * BN + col_base;
 
             if (col_params && !warp_wait(&pready[acc], aph, abort_flag, p.status,
                                          GK_DEV_TIMEOUT_EPILOGUE, tmo))
@@ -361,14 +403,17 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
 
             const int t_next = t + npairs;
             Raw raw_next;
-            if (C::QUANT && t_next < n_items) load_raw(t_next, raw_next);
+            if (C::QUANT && t_next < n_items) load_raw(locate(t_next), raw_next);
 
             const int64_t obase = static_cast<int64_t>(b) * e.obs + grow * e.ldo;
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + col_base);
             // the requantize path for this tile's rows, then the chunk loop compiled for it
             int qm = QM_GENERAL;
-            if constexpr (C::QUANT) qm = pick_quant_mode(e, r_se);
+            if constexpr (C::QUANT) {
+                qm = pick_quant_mode(e, r_se);
+                if (qm == QM_GENERAL && e.scale_axis != AX_N) make_scale_clamp(r_se, r_ulo, r_uhi);
+            }
             auto chunks = [&](auto qm_tag) {
                 constexpr int QM = decltype(qm_tag)::value;
                 uint32_t va[32], vb[32];
@@ -398,12 +443,14 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
                     }
                     if (row_ok)
                         epilogue_chunk<OUT, CH, QM>(cur, p.Nk, e, obase, gc, cp + col_base + c * CH,
-                                                cbias + acc * BN + col_base + c * CH, r_se,
-                                                r_nms, r_ulo, r_uhi, r_bp, r_fb);
+                                                    cb + c * CH, r_se, r_nms, r_ulo, r_uhi, r_bp,
+                                                    r_fb);
                 }
             };
             with_quant_mode<C::QUANT>(qm, chunks);
-            if (C::QUANT && t_next < n_items) commit(raw_next, acc ^ 1);
+            // (the next item is located again rather than kept live across the chunk loop)
+            if (t_next < n_items) pos = locate(t_next);
+            if (C::QUANT && t_next < n_items) commit(raw_next, pos, acc ^ 1);
         }
     }
 
@@ -454,6 +501,7 @@ static int launch_pair_one(const TcProblem& pr, const TcPlan& plan, GemmParams g
     }
     gp.tiles_n = plan.tiles_n;
     gp.tiles_per_batch = gp.tiles_m * gp.tiles_n;
+    set_tile_divs(&gp);
     gp.num_tiles = plan.num_tiles;
     gp.dp_tiles = plan.num_tiles;
 

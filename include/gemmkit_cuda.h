@@ -195,10 +195,11 @@ int gk_gemm_i8_packed_b_requant_unchecked(gk_workspace *ws, size_t m, const int8
 
 /* The decode-step GEMV. gemmkit reaches its small-shape route only from inside dispatch
  * (special/small_mn.rs:834-1060, gated at dispatch.rs:438-482); this entry names it:
- * C = requant(A * packedB) for 1 <= m <= 64 activation rows, on the bandwidth-bound small-M
- * kernel that streams the prepacked weights once from HBM (unless GEMMKIT_CUDA_GEMV=0).
- * Arguments and results as gk_gemm_i8_packed_b_requant_unchecked; m outside [1, 64] is
- * GK_EINVAL. */
+ * C = requant(A * packedB) for 1 <= m <= 64 activation rows. When the packed side is the
+ * wider one (n > m) this runs on the bandwidth-bound small-M kernel that streams the
+ * prepacked weights once from HBM (unless GEMMKIT_CUDA_GEMV=0); when n <= m both sides are
+ * at most 64 wide and the product goes to the general tile kernel. Arguments and results as
+ * gk_gemm_i8_packed_b_requant_unchecked; m outside [1, 64] is GK_EINVAL. */
 int gk_gemv_i8_requant_unchecked(gk_workspace *ws, size_t m, const int8_t *a, ptrdiff_t rsa,
                                  ptrdiff_t csa, const gk_packed_rhs *packed,
                                  const gk_requant *req, void *c, ptrdiff_t rsc, ptrdiff_t csc,
@@ -284,6 +285,26 @@ int gk_gemm_half_f32_fused(gk_workspace *ws, int is_f16, float alpha, gk_matref 
                            float beta, gk_matmut c, const float *bias, size_t bias_len,
                            int bias_dim, int act, float leak, gk_parallelism par,
                            gk_stream_t stream);
+
+/* ---- fused i32 epilogue on the i8 -> i32 GEMM ------------------------------------------ */
+
+/* The integer counterpart of gk_gemm_half_f32_fused: C = act(alpha*A*B + beta*C + bias) with
+ * i8 operands and i32 C, every step wrapping mod 2^32 as gemmkit's int32_epilogue does
+ * (gemmkit/src/kernel/int.rs:36-120), the i32 bias per row (length m) or per column (length
+ * n), then ReLU as max(v, 0) on the signed value. gemmkit's FusedEpi (gemmkit/src/kernel/
+ * epilogue.rs:258-330) composes bias-then-activation for float GEMMs only; this entry applies
+ * the same composition to gemm_i8 (gemmkit/src/api/int8.rs:136-178) inside the GEMM's
+ * epilogue. act is GK_ACT_NONE or GK_ACT_RELU (GK_ACT_LEAKY_RELU is GK_EINVAL: its slope is a
+ * float). With k == 0 or alpha == 0, C <- act(beta*C + bias). The checked tier validates the
+ * views like gk_gemm_i8 and the bias length like gk_gemm_half_f32_fused. */
+int gk_gemm_i8_fused_unchecked(gk_workspace *ws, size_t m, size_t k, size_t n, int32_t alpha,
+                               const int8_t *a, ptrdiff_t rsa, ptrdiff_t csa, const int8_t *b,
+                               ptrdiff_t rsb, ptrdiff_t csb, int32_t beta, int32_t *c,
+                               ptrdiff_t rsc, ptrdiff_t csc, const int32_t *bias, int bias_dim,
+                               int has_bias, int act, gk_parallelism par, gk_stream_t stream);
+int gk_gemm_i8_fused(gk_workspace *ws, int32_t alpha, gk_matref a, gk_matref b, int32_t beta,
+                     gk_matmut c, const int32_t *bias, size_t bias_len, int bias_dim, int act,
+                     gk_parallelism par, gk_stream_t stream);
 
 /* ---- producer step: f32 activations -> i8 (no counterpart in gemmkit) ---------------- */
 

@@ -163,6 +163,23 @@ def gemm_i8_matrix(alpha: int, a: np.ndarray, b: np.ndarray, beta: int,
     return out
 
 
+def gemm_i8_fused_matrix(alpha: int, a: np.ndarray, b: np.ndarray, beta: int,
+                         c: np.ndarray | None = None, bias: np.ndarray | None = None,
+                         bias_axis: str = "row", relu: bool = False) -> np.ndarray:
+    """act(alpha*A*B + beta*C + bias) for the fused i32 epilogue (an engine extension): the
+    scalar restatement of int32_epilogue (gko_gemm_i8) followed by the bias-then-activation
+    composition of gemmkit's FusedEpi::apply (gemmkit/src/kernel/epilogue.rs:300-330), here in
+    wrapping i32: v + bias mod 2^32, then ReLU as max(v, 0)."""
+    out = gemm_i8_matrix(alpha, a, b, beta, c).astype(np.int64)
+    if bias is not None:
+        bv = np.asarray(bias, dtype=np.int64)
+        out = out + (bv[:, None] if bias_axis == "row" else bv[None, :])
+        out = ((out + 2**31) % 2**32) - 2**31
+    if relu:
+        out = np.maximum(out, 0)
+    return out.astype(np.int32)
+
+
 def f32_to_bf16(x: np.ndarray) -> np.ndarray:
     """Round-to-nearest-even f32 -> bf16 bit patterns (uint16), NaN kept quiet."""
     u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)

@@ -236,7 +236,7 @@ def test_knobs_get_set_and_validation():
     import gemmkit_b200 as gk
     names = gk.knob_names()
     assert names == ["GEMMKIT_CUDA_BN", "GEMMKIT_CUDA_PAIR", "GEMMKIT_CUDA_GEMV",
-                     "GEMMKIT_CUDA_PDL", "GEMMKIT_CUDA_STREAMK"]
+                     "GEMMKIT_CUDA_PDL", "GEMMKIT_CUDA_STREAMK", "GEMMKIT_CUDA_GEMV_SK"]
     base = {n: gk.knob_get(n) for n in names}
     try:
         gk.knob_set("GEMMKIT_CUDA_BN", 128)
@@ -270,6 +270,31 @@ def test_fused_bias_validation_without_gpu():
                                               C.c_void_p(16), 4, 1, 0.0, C.c_void_p(16), 4, 1,
                                               None, 1, 0, 7, 0.0, _lib.Parallelism(0, 0), None)
     assert rc == _lib.GK_EINVAL and b"unknown activation 7" in lib.gk_last_error()
+
+
+def test_fused_i32_validation_without_gpu():
+    """The fused i32 entries reject a LeakyReLU (its slope is a float), an unknown activation,
+    a bias dimension that is neither row nor column, and (checked tier) a bias whose length
+    does not follow its dimension -- all before any device work."""
+    a = gk.MatRef.new((16, 6), 2, 3, 3, 1)
+    b = gk.MatRef.new((16, 12), 3, 4, 4, 1)
+    c = gk.MatMut.new((64, 8), 2, 4, 4, 1)
+    with pytest.raises(gk.GemmkitError, match="per-column bias length 3 does not match n = 4"):
+        gk.gemm_i8_fused(1, a, b, 0, c, bias=(128, 3), bias_dim=gk.AXIS_COL)
+    with pytest.raises(gk.GemmkitError, match="per-row bias length 4 does not match m = 2"):
+        gk.gemm_i8_fused(1, a, b, 0, c, bias=(128, 4), bias_dim=gk.AXIS_ROW)
+    with pytest.raises(gk.GemmkitError, match="no LeakyReLU"):
+        gk.gemm_i8_fused(1, a, b, 0, c, act=gk.Activation.LeakyRelu(0.1))
+    lib = _lib.load()
+    args = (None, 2, 3, 4, 1, C.c_void_p(16), 3, 1, C.c_void_p(16), 4, 1, 0, C.c_void_p(16), 4,
+            1)
+    rc = lib.gk_gemm_i8_fused_unchecked(*args, None, 1, 0, 9, _lib.Parallelism(0, 0), None)
+    assert rc == _lib.GK_EINVAL and b"unknown activation 9" in lib.gk_last_error()
+    rc = lib.gk_gemm_i8_fused_unchecked(*args, C.c_void_p(16), 5, 1, 1, _lib.Parallelism(0, 0),
+                                        None)
+    assert rc == _lib.GK_EINVAL and b"bias dimension" in lib.gk_last_error()
+    rc = lib.gk_gemm_i8_fused_unchecked(*args, None, 1, 1, 1, _lib.Parallelism(0, 0), None)
+    assert rc == _lib.GK_EINVAL and b"null bias" in lib.gk_last_error()
 
 
 def test_quantize_argument_errors_without_gpu():

@@ -181,3 +181,24 @@ def test_gemv_entry(M, out_u8):
         gk.gemm_i8_packed_b_requant(M, ptr(da), k, 1, packed, req, ptr(dref), rsc, csc,
                                     out_u8=out_u8)
         assert np.array_equal(host(dc), host(dref))
+
+
+@pytest.mark.parametrize("m,n", [(64, 40), (17, 17), (33, 5)])
+def test_gemv_entry_packed_side_not_wider(m, n):
+    """gk_gemv_i8_requant_unchecked with n <= m <= 64 (both sides small; the general tile
+    kernel takes it): bit-exact against the oracle in both C orientations."""
+    k = 1000
+    rng = np.random.default_rng(m * 100 + n)
+    a = rand_i8(rng, (m, k), -127, 127)
+    bT = rand_i8(rng, (n, k), -127, 127)
+    scales = rng.uniform(1e-4, 1e-3, n).astype(np.float32)
+    bias = rng.integers(-3000, 3000, n).astype(np.int32)
+    want = O.requant_matrix(a, bT.T, scales=scales, scale_axis="col", bias=bias,
+                            bias_axis="col", zp=2, relu=True)
+    packed = gk.prepack_rhs_i8(gk.MatRef.new(dev(bT), k, n, 1, k))
+    req = gk.Requantize(gk.RequantScale.PerCol(dev(scales)), 2, dev(bias), gk.AXIS_COL, True)
+    da = dev(a)
+    for rsc, csc in ((n, 1), (1, m)):
+        dc = empty(m * n, np.int8)
+        gk.gemv_i8_requant(m, ptr(da), k, 1, packed, req, ptr(dc), rsc, csc)
+        assert np.array_equal(gather(host(dc), m, n, rsc, csc), want), (rsc, csc)

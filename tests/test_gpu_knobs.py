@@ -38,6 +38,7 @@ def vnni_requant(a, bT, out_u8=False, **req):
 
 
 KNOB_SETS = [
+    dict(GEMMKIT_CUDA_GEMV_SK=1),
     dict(GEMMKIT_CUDA_PDL=0),
     dict(GEMMKIT_CUDA_PAIR=0, GEMMKIT_CUDA_STREAMK=0),
     dict(GEMMKIT_CUDA_GEMV=0),
@@ -88,7 +89,7 @@ def test_knob_paths_requant_and_i32(kv):
     assert np.array_equal(host(di).reshape(m, n), want_i32)
 
 
-@pytest.mark.parametrize("kv", KNOB_SETS[:3], ids=_kid)
+@pytest.mark.parametrize("kv", KNOB_SETS[1:4], ids=_kid)
 def test_knob_paths_batched_requant(kv):
     rng = np.random.default_rng(11)
     batch, m, n, k = 24, 512, 512, 128
@@ -96,10 +97,11 @@ def test_knob_paths_batched_requant(kv):
     bT = rand_i8(rng, (batch, n, k))
     bias = rng.integers(-2**15, 2**15 + 1, (batch, m)).astype(np.int32)
     scales = rng.uniform(1e-4, 1e-3, (batch, n)).astype(np.float32)
-    req = gk.Requantize(gk.RequantScale.PerCol(dev(scales)), 128, dev(bias), gk.AXIS_ROW)
+    da, dbT, dsc, dbias = dev(a), dev(bT), dev(scales), dev(bias)  # held until the call ends
+    req = gk.Requantize(gk.RequantScale.PerCol(dsc), 128, dbias, gk.AXIS_ROW)
     dc = empty(batch * m * n, np.uint8)
     with knobs(**kv):
-        gk.gemm_i8_requant_batched(batch, m, k, n, ptr(dev(a)), k, 1, m * k, ptr(dev(bT)), 1, k,
+        gk.gemm_i8_requant_batched(batch, m, k, n, ptr(da), k, 1, m * k, ptr(dbT), 1, k,
                                    n * k, req, m, n, ptr(dc), 1, m, m * n, out_u8=True)
     got = host(dc).reshape(batch, n, m)
     for e in range(batch):
@@ -132,9 +134,9 @@ def test_pair_epi16_requant(shape, axes, out_u8):
     zp = (128 if out_u8 else -5) + (rng.integers(0, 2) if scale_axis == "row" else 0)
     want = vnni_requant(a, bT, scales=scales, scale_axis=scale_axis, bias=bias,
                         bias_axis=bias_axis, zp=int(zp), out_u8=out_u8, relu=True)
-    da, dbT = dev(a), dev(bT)
-    sc = gk.RequantScale(0.0, dev(scales), gk.AXIS_ROW if scale_axis == "row" else gk.AXIS_COL)
-    req = gk.Requantize(sc, int(zp), dev(bias),
+    da, dbT, dsc, dbias = dev(a), dev(bT), dev(scales), dev(bias)
+    sc = gk.RequantScale(0.0, dsc, gk.AXIS_ROW if scale_axis == "row" else gk.AXIS_COL)
+    req = gk.Requantize(sc, int(zp), dbias,
                         gk.AXIS_ROW if bias_axis == "row" else gk.AXIS_COL, True)
     for c_row in (True, False):
         dc = empty(m * n, np.uint8 if out_u8 else np.int8)
@@ -143,3 +145,28 @@ def test_pair_epi16_requant(shape, axes, out_u8):
                                         rsc, csc, out_u8=out_u8)
         got = gather(host(dc), m, n, rsc, csc)
         assert np.array_equal(got, want), (c_row, axes)
+
+
+@pytest.mark.parametrize("sk", [0, 1])
+def test_small_m_config5_both_modes(sk):
+    """BASELINE config 5 (M = 1, 4, 16 over a 4096 x 14336 prepacked B) with the small-M
+    kernel's weight stream in whole tiles and in the even stream-K split, three calls in a row
+    (the partial counters' epochs), bit-exact against the oracle."""
+    rng = np.random.default_rng(55 + sk)
+    k, n = 4096, 14336
+    bT = rand_i8(rng, (n, k), -127, 127)
+    scales = rng.uniform(1e-4, 1e-3, n).astype(np.float32)
+    bias = rng.integers(-2**15, 2**15 + 1, n).astype(np.int32)
+    dbT, dsc, dbias = dev(bT), dev(scales), dev(bias)
+    packed = gk.prepack_rhs_i8(gk.MatRef.new(dbT, k, n, 1, k))
+    req = gk.Requantize(gk.RequantScale.PerCol(dsc), -3, dbias, gk.AXIS_COL, True)
+    with knobs(GEMMKIT_CUDA_GEMV_SK=sk):
+        for M in (1, 4, 16):
+            a = rand_i8(rng, (M, k), -127, 127)
+            want = vnni_requant(a, bT, scales=scales, scale_axis="col", bias=bias,
+                                bias_axis="col", zp=-3, relu=True)
+            da = dev(a)
+            for _ in range(3):
+                dc = empty(M * n, np.int8)
+                gk.gemm_i8_packed_b_requant(M, ptr(da), k, 1, packed, req, ptr(dc), n, 1)
+                assert np.array_equal(host(dc).reshape(M, n), want), (M, sk)
