@@ -76,8 +76,9 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, local_index: int):
+    def __init__(self, local_index: int, interval_s: float = 0.01):
         self.local = local_index
+        self.interval = interval_s
         self.samples: list[tuple[float, int, float]] = []  # (sm MHz, reasons mask, W)
         self.smax = None
         self.proc = None
@@ -111,7 +112,7 @@ class ClockSampler:
                         self.samples.append((float(sm), int(rs), pw))
                     except Exception:
                         pass
-                    self._stop.wait(0.01)
+                    self._stop.wait(self.interval)
             self.t = threading.Thread(target=loop, daemon=True)
             self.t.start()
             return
@@ -143,7 +144,7 @@ class ClockSampler:
             return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
                     "sm_mhz_min": min(sm) if sm else None, "reasons": reasons,
                     "power_w_max": round(max(x[2] for x in self.samples), 1) if sm else None,
-                    "samples": len(sm), "source": "nvml, 10 ms"}
+                    "samples": len(sm), "source": f"nvml, {self.interval * 1e3:g} ms"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
         self.proc.terminate()
@@ -879,12 +880,13 @@ def main():
         w.step(i)
     torch.cuda.synchronize()
     barrier(ws)
-    # Clock record: NVML samples every 10 ms from the start of a ~100 ms pre-roll of the same
+    # Clock record: NVML samples every 2 ms from the start of a ~20 ms pre-roll of the same
     # step (untimed, at the load of the timed region) through the end of the timed region, so
-    # the record holds several samples even when the timed region is ~1 ms.
+    # the record holds several samples even when the timed region is ~1 ms. (A longer pre-roll
+    # already brings the 1 kW power cap into the timed steps.)
     est_ms = time_steps(w.step, 20, 0, 1) / 20
-    preroll = int(min(5000, max(0, 100.0 / max(est_ms, 1e-3))))
-    sampler = ClockSampler(local) if rank == 0 else None
+    preroll = int(min(2000, max(0, 20.0 / max(est_ms, 1e-3))))
+    sampler = ClockSampler(local, 0.002) if rank == 0 else None
     barrier(ws)
     if sampler:
         sampler.start()

@@ -88,16 +88,29 @@ int check_device(int* dev_out) {
 //   GEMMKIT_CUDA_GEMV_SK  1 = the small-M kernel splits its weight stream evenly over all SMs
 //                         (stream-K partials in the workspace) when whole tiles would not;
 //                         off by default (measured slower than whole tiles on config 5)
-enum KnobId { K_BN = 0, K_PAIR, K_GEMV, K_PDL, K_STREAMK, K_GEMVSK, K_COUNT };
-const char* const kKnobEnv[K_COUNT] = {"GEMMKIT_CUDA_BN",   "GEMMKIT_CUDA_PAIR",
-                                       "GEMMKIT_CUDA_GEMV", "GEMMKIT_CUDA_PDL",
-                                       "GEMMKIT_CUDA_STREAMK", "GEMMKIT_CUDA_GEMV_SK"};
-const int64_t kKnobDefault[K_COUNT] = {0, 1, 1, 1, 0, 0};
+//   GEMMKIT_CUDA_BN_SHORTK tile width for products whose K is at most 256 bytes (one or two
+//                         128-byte blocks: epilogue-bound); 0 = the GEMMKIT_CUDA_BN rule
+//   GEMMKIT_CUDA_EPI16    1 = the CTA-pair kernel takes its 16-warp epilogue form for short K
+//   GEMMKIT_CUDA_STAGES   shared-memory ring depth cap of the kernels (0 = their whole ring,
+//                         else 2 .. 12)
+//   GEMMKIT_CUDA_GEMV_SPLIT largest cluster K split of the small-M kernel (0 = up to 8)
+enum KnobId {
+    K_BN = 0, K_PAIR, K_GEMV, K_PDL, K_STREAMK, K_GEMVSK, K_BNSHORTK, K_EPI16, K_STAGES,
+    K_GEMVSPLIT, K_COUNT
+};
+const char* const kKnobEnv[K_COUNT] = {
+    "GEMMKIT_CUDA_BN",       "GEMMKIT_CUDA_PAIR",      "GEMMKIT_CUDA_GEMV",
+    "GEMMKIT_CUDA_PDL",      "GEMMKIT_CUDA_STREAMK",   "GEMMKIT_CUDA_GEMV_SK",
+    "GEMMKIT_CUDA_BN_SHORTK", "GEMMKIT_CUDA_EPI16",    "GEMMKIT_CUDA_STAGES",
+    "GEMMKIT_CUDA_GEMV_SPLIT"};
+const int64_t kKnobDefault[K_COUNT] = {0, 1, 1, 1, 0, 0, 0, 1, 0, 0};
 std::atomic<int64_t> g_knob_set[K_COUNT];  // value + 1; 0 = no run-time override
 
 bool knob_valid(int id, int64_t v) {
-    if (id == K_BN)
+    if (id == K_BN || id == K_BNSHORTK)
         return v == 0 || v == 16 || v == 32 || v == 64 || v == 128 || v == 192 || v == 256;
+    if (id == K_STAGES) return v == 0 || (v >= 2 && v <= 12);
+    if (id == K_GEMVSPLIT) return v >= 0 && v <= 8;
     return v == 0 || v == 1;
 }
 
@@ -135,8 +148,12 @@ bool gemv_enabled() { return knob(K_GEMV) == 1; }
 bool pdl_enabled() { return knob(K_PDL) == 1; }
 bool gemv_sk_enabled() { return knob(K_GEMVSK) == 1; }
 
-int tile_n_override() {
+int tile_n_override(int64_t k_bytes = -1) {
     if (g_tile_n >= 0) return g_tile_n;
+    if (k_bytes >= 0 && k_bytes <= 256) {
+        const int64_t v = knob(K_BNSHORTK);
+        if (v) return static_cast<int>(v);
+    }
     return static_cast<int>(knob(K_BN));
 }
 
@@ -530,9 +547,12 @@ int execute(const Job& j) {
     pr.K = j.k;
     pr.batch = j.batch;
     pr.e = e;
-    pr.bn = tile_n_override();
+    pr.bn = tile_n_override(j.k * es);
     pr.stream = j.stream;
     pr.pdl = pdl_enabled() ? 1 : 0;
+    pr.stages = static_cast<int>(knob(K_STAGES));
+    pr.epi16 = static_cast<int>(knob(K_EPI16));
+    pr.gemv_split = static_cast<int>(knob(K_GEMVSPLIT));
     // the planners look at which operand is in the tiled prepacked layout; the operands
     // themselves are filled in below, once any packing has its scratch
     pr.a.slab = ka.slab;
@@ -663,7 +683,8 @@ void gk_workspace_free(gk_workspace* ws) {
 
 const char* gk_knob_names(void) {
     return "GEMMKIT_CUDA_BN,GEMMKIT_CUDA_PAIR,GEMMKIT_CUDA_GEMV,GEMMKIT_CUDA_PDL,"
-           "GEMMKIT_CUDA_STREAMK,GEMMKIT_CUDA_GEMV_SK";
+           "GEMMKIT_CUDA_STREAMK,GEMMKIT_CUDA_GEMV_SK,GEMMKIT_CUDA_BN_SHORTK,GEMMKIT_CUDA_EPI16,"
+           "GEMMKIT_CUDA_STAGES,GEMMKIT_CUDA_GEMV_SPLIT";
 }
 
 int gk_knob_get(const char* name, int64_t* value) {

@@ -82,6 +82,7 @@ struct GemmParams {
     uint32_t sk_epoch;
     uint64_t timeout_ns;
     unsigned int* status;
+    int32_t stages;  // ring depth cap (0: the kernel's whole ring)
     EpiParams e;
 };
 
@@ -107,6 +108,9 @@ struct TcProblem {
     int bn;  // 0 = heuristic
     cudaStream_t stream;
     int pdl;  // 1: kernels that support it may overlap the previous kernel of the stream
+    int stages;  // ring depth cap of the kernels (0: their whole ring)
+    int epi16;   // 1: the CTA-pair kernel may take its 16-warp epilogue form (short K)
+    int gemv_split;  // small-M kernel: largest cluster K split (0: up to 8)
     // Scratch for a stream-K tail (see GemmParams); nullptr = no stream-K.
     uint32_t* sk_part;
     uint32_t* sk_ctr;

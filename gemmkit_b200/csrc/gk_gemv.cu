@@ -68,6 +68,7 @@ struct GemvParams {
     int64_t w_slab;          // bytes between consecutive K blocks of w_tiled
     uint64_t timeout_ns;
     unsigned int* status;
+    int32_t stages;  // ring depth cap (0: the whole ring)
     EpiParams e;
 };
 
@@ -101,22 +102,30 @@ struct GemvCfg {
     static_assert((2 * STAGES + 2 * NACC + 1) * 8 + 8 <= BAR_BYTES, "barrier area");
 };
 
-// One work item of a CTA: K blocks [k0, k1) of `tile`; nctr > 1 marks a tile shared with
-// other CTAs (stream-K), of which this CTA holds partial slot `slot`.
+// One work item of a CTA: K blocks [k0, k1) of `tile`. In stream-K mode a tile shared by
+// nctr CTAs (consecutive in blockIdx) is finished by the highest-numbered of them, its
+// finisher; the others are writers and publish 32-bit partial accumulators in slot
+// (CTA - first CTA of the tile). role: GEMV_WHOLE, GEMV_WRITER or GEMV_FINISHER.
+enum : int { GEMV_WHOLE = 0, GEMV_WRITER = 1, GEMV_FINISHER = 2 };
 struct GemvItem {
-    int tile, k0, k1, slot, nctr;
+    int tile, k0, k1, slot, nctr, role;
 };
 
 // The CTA's work items, identical for every role.
 //  * split > 1: K blocks [r*num_kb/split, (r+1)*num_kb/split) of tile blockIdx.x / split,
 //    r = blockIdx.x % split (the CTA's rank in its cluster);
-//  * sk: the CTA's run [s, e) of units; first the pieces of the (at most two) tiles it shares
-//    with its neighbours, then the tiles it covers whole, so that every shared tile is
-//    finished early by all of its CTAs and its reduction overlaps the rest of the streaming;
+//  * sk: the CTA's run [s, e) of the units. Its run ends inside a tile it shares with the next
+//    CTAs (it writes that tile's first K blocks: a writer piece) and starts inside a tile it
+//    shares with the previous CTAs (it holds that tile's last K blocks: the finisher piece).
+//    Order: the writer piece first, the whole tiles, the finisher piece last. A finisher
+//    therefore waits only on lower-numbered CTAs, which have long finished their first item,
+//    and it collects their partials while its own last MMAs run, so no reduction sits at the
+//    end of the call;
 //  * otherwise whole tiles blockIdx.x, blockIdx.x + gridDim.x, ...
 struct GemvSched {
-    int nsh, w_lo, w_cnt;
-    GemvItem sh0, sh1;  // the shared pieces (two members, not an array: no local memory)
+    int w_lo, w_cnt;
+    bool has_wr, has_fin;
+    GemvItem wr, fin;
 
     __device__ __forceinline__ static int64_t start(const GemvParams& p, int c) {
         return static_cast<int64_t>(c) * p.units / static_cast<int64_t>(gridDim.x);
@@ -127,33 +136,42 @@ struct GemvSched {
         const int64_t c = ((T + 1) * G + p.units - 1) / p.units - 1;
         return static_cast<int>(c < 0 ? 0 : (c >= G ? G - 1 : c));
     }
-    __device__ __forceinline__ void shared_piece(const GemvParams& p, int tile, int k0, int k1) {
+    __device__ __forceinline__ static GemvItem piece(const GemvParams& p, int tile, int k0, int k1,
+                                                     int role) {
         const int64_t t0 = static_cast<int64_t>(tile) * p.num_kb;
         const int cf = owner(p, t0), cl = owner(p, t0 + p.num_kb - 1);
-        const GemvItem it{tile, k0, k1, static_cast<int>(blockIdx.x) - cf, cl - cf + 1};
-        if (nsh == 0)
-            sh0 = it;
-        else
-            sh1 = it;
-        ++nsh;
+        return GemvItem{tile, k0, k1, static_cast<int>(blockIdx.x) - cf, cl - cf + 1, role};
     }
     __device__ __forceinline__ explicit GemvSched(const GemvParams& p) {
-        nsh = 0;
         w_lo = 0;
         w_cnt = 0;
-        sh0 = sh1 = GemvItem{0, 0, 0, 0, 1};
+        has_wr = has_fin = false;
+        wr = fin = GemvItem{0, 0, 0, 0, 1, GEMV_WHOLE};
         if (!p.sk) return;
         const int nkb = p.num_kb;
         const int64_t s = start(p, blockIdx.x), e = start(p, blockIdx.x + 1);
         if (e <= s) return;
         const int tA = static_cast<int>(s / nkb), tB = static_cast<int>((e - 1) / nkb);
         const int sA = static_cast<int>(s - static_cast<int64_t>(tA) * nkb);
-        const int64_t eA = e - static_cast<int64_t>(tA) * nkb;
-        if (sA != 0) shared_piece(p, tA, sA, eA < nkb ? static_cast<int>(eA) : nkb);
-        const int eB = static_cast<int>(e - static_cast<int64_t>(tB) * nkb);
-        if (eB != nkb && !(tB == tA && sA != 0)) {
-            const int64_t sB = s - static_cast<int64_t>(tB) * nkb;
-            shared_piece(p, tB, sB > 0 ? static_cast<int>(sB) : 0, eB);
+        const int eB = static_cast<int>(e - static_cast<int64_t>(tB) * nkb);  // 1 .. nkb
+        if (tA == tB) {
+            // the run lies inside one tile: [sA, eB)
+            if (eB < nkb) {
+                has_wr = true;
+                wr = piece(p, tA, sA, eB, GEMV_WRITER);
+            } else if (sA > 0) {
+                has_fin = true;
+                fin = piece(p, tA, sA, nkb, GEMV_FINISHER);
+            }
+        } else {
+            if (sA > 0) {
+                has_fin = true;
+                fin = piece(p, tA, sA, nkb, GEMV_FINISHER);
+            }
+            if (eB < nkb) {
+                has_wr = true;
+                wr = piece(p, tB, 0, eB, GEMV_WRITER);
+            }
         }
         w_lo = static_cast<int>((s + nkb - 1) / nkb);
         const int w_hi = static_cast<int>(e / nkb) - 1;
@@ -161,12 +179,19 @@ struct GemvSched {
     }
     __device__ __forceinline__ bool get(const GemvParams& p, int idx, GemvItem& it) const {
         if (p.sk) {
-            if (idx < nsh) {
-                it = idx == 0 ? sh0 : sh1;
+            if (has_wr) {
+                if (idx == 0) {
+                    it = wr;
+                    return true;
+                }
+                --idx;
+            }
+            if (idx < w_cnt) {
+                it = GemvItem{w_lo + idx, 0, p.num_kb, 0, 1, GEMV_WHOLE};
                 return true;
             }
-            if (idx - nsh < w_cnt) {
-                it = GemvItem{w_lo + idx - nsh, 0, p.num_kb, 0, 1};
+            if (has_fin && idx == w_cnt) {
+                it = fin;
                 return true;
             }
             return false;
@@ -177,13 +202,62 @@ struct GemvSched {
             const int r = static_cast<int>(blockIdx.x) - tile * p.split;
             it = GemvItem{tile, static_cast<int>(static_cast<int64_t>(r) * p.num_kb / p.split),
                           static_cast<int>(static_cast<int64_t>(r + 1) * p.num_kb / p.split), 0,
-                          1};
+                          1, GEMV_WHOLE};
             return true;
         }
         const int tile = static_cast<int>(blockIdx.x) + idx * static_cast<int>(gridDim.x);
         if (tile >= p.tiles) return false;
-        it = GemvItem{tile, 0, p.num_kb, 0, 1};
+        it = GemvItem{tile, 0, p.num_kb, 0, 1, GEMV_WHOLE};
         return true;
+    }
+};
+
+// The CTA's stages in streaming order, the same for the producer and the MMA issuer: item
+// by item (whole tiles, cluster split), or in stream-K mode K block by K block across the
+// CTA's items (at most GemvCfg::NACC), so that at any moment every CTA reads the same K-block
+// slab of the weights (the slabs are contiguous in the tiled prepacked layout) and each item
+// accumulates in its own TMEM accumulator.
+struct GemvStage {
+    int item, tile, kb, k0, k1;
+};
+struct GemvStages {
+    int item, kb, nitems;
+    __device__ __forceinline__ GemvStages(const GemvParams& p, const GemvSched& sch) {
+        item = 0;
+        kb = -1;
+        nitems = p.sk ? (sch.has_wr ? 1 : 0) + sch.w_cnt + (sch.has_fin ? 1 : 0) : 0;
+    }
+    __device__ __forceinline__ bool next(const GemvParams& p, const GemvSched& sch, GemvStage& st) {
+        GemvItem it;
+        if (!p.sk) {
+            while (true) {
+                if (!sch.get(p, item, it)) return false;
+                kb = kb < 0 ? it.k0 : kb + 1;
+                if (kb < it.k1) {
+                    st = GemvStage{item, it.tile, kb, it.k0, it.k1};
+                    return true;
+                }
+                ++item;
+                kb = -1;
+            }
+        }
+        if (kb < 0) {
+            kb = 0;
+            item = 0;
+        }
+        while (kb < p.num_kb) {
+            while (item < nitems) {
+                const int j = item++;
+                sch.get(p, j, it);
+                if (it.k0 <= kb && kb < it.k1) {
+                    st = GemvStage{j, it.tile, kb, it.k0, it.k1};
+                    return true;
+                }
+            }
+            item = 0;
+            ++kb;
+        }
+        return false;
     }
 };
 
@@ -197,6 +271,10 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
                 const GemvParams p) {
     using C = GemvCfg<NB>;
     constexpr int STAGES = C::STAGES;
+    // The ring depth is the kernel's whole ring: the single-thread producer and MMA loops are
+    // on the critical path of the streaming (each stage's turnaround bounds the bytes in
+    // flight), and a run-time modulus measured slower; GEMMKIT_CUDA_STAGES does not apply.
+    constexpr int nst = STAGES;
     constexpr int ES = (KIND == Kind::I8) ? 1 : 2;
     constexpr int BKE = BKB / ES;
     constexpr bool QUANT = OUT == Out::Q8 || OUT == Out::U8;
@@ -271,38 +349,69 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
             };
             // The first ring of weight blocks, ahead of the grid dependency (prepacked only).
             const GemvSched sch(p);
-            GemvItem wi;
+            GemvStage sg;
             int pre = 0;
             if (p.early_weights && p.w_tiled) {
-                for (int n = 0; pre < STAGES && sch.get(p, n, wi); ++n)
-                    for (int kb = wi.k0; kb < wi.k1 && pre < STAGES; ++kb, ++pre) {
-                        mbar_arrive_expect_tx(&full[pre], C::STAGE_BYTES);
-                        issue_w(pre, wi.tile, kb);
-                    }
+                GemvStages it0(p, sch);
+                for (; pre < nst && it0.next(p, sch, sg); ++pre) {
+                    mbar_arrive_expect_tx(&full[pre], C::STAGE_BYTES);
+                    issue_w(pre, sg.tile, sg.kb);
+                }
             }
             griddep_wait();
             int stage = 0, idx = 0;
             uint32_t phase = 0, issued = 0, last_par = 0;
-            bool ok = true;
-            for (int n = 0; ok && sch.get(p, n, wi); ++n) {
-                const int tile = wi.tile;
-                for (int kb = wi.k0; kb < wi.k1; ++kb, ++idx) {
+            if (!p.sk) {
+                // item by item (kept as plain loops: this thread's per-stage turnaround is on
+                // the streaming's critical path)
+                GemvItem wi;
+                bool ok = true;
+                for (int n = 0; ok && sch.get(p, n, wi); ++n) {
+                    const int tile = wi.tile;
+                    for (int kb = wi.k0; kb < wi.k1; ++kb, ++idx) {
+                        if (idx >= pre) {
+                            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status,
+                                           GK_DEV_TIMEOUT_PRODUCER, tmo)) {
+                                ok = false;
+                                break;
+                            }
+                            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                            issue_w(stage, tile, kb);
+                        }
+                        tma_load_3d(sX + stage * C::X_BYTES, &tmX, &full[stage], kb * BKE, 0, 0);
+                        issued |= 1u << stage;
+                        last_par = (last_par & ~(1u << stage)) | (phase << stage);
+                        if (++stage == nst) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                }
+            } else {
+                auto one = [&](int tile, int kb) {
                     if (idx >= pre) {
                         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status,
-                                       GK_DEV_TIMEOUT_PRODUCER, tmo)) {
-                            ok = false;
-                            break;
-                        }
+                                       GK_DEV_TIMEOUT_PRODUCER, tmo))
+                            return false;
                         mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
                         issue_w(stage, tile, kb);
                     }
                     tma_load_3d(sX + stage * C::X_BYTES, &tmX, &full[stage], kb * BKE, 0, 0);
                     issued |= 1u << stage;
                     last_par = (last_par & ~(1u << stage)) | (phase << stage);
-                    if (++stage == STAGES) {
+                    if (++stage == nst) {
                         stage = 0;
                         phase ^= 1u;
                     }
+                    ++idx;
+                    return true;
+                };
+                // stream-K: K block by K block across the items (writer, whole tiles, finisher)
+                bool ok = true;
+                for (int kb = 0; kb < p.num_kb && ok; ++kb) {
+                    if (sch.has_wr && kb >= sch.wr.k0 && kb < sch.wr.k1) ok = one(sch.wr.tile, kb);
+                    for (int j = 0; j < sch.w_cnt && ok; ++j) ok = one(sch.w_lo + j, kb);
+                    if (ok && sch.has_fin && kb >= sch.fin.k0) ok = one(sch.fin.tile, kb);
                 }
             }
             // This CTA has asked for all its data: the next kernel of the stream may start
@@ -327,28 +436,63 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
             else
                 idesc = idesc_f16(BM, NB, KIND == Kind::BF16);
             const GemvSched sch(p);
-            GemvItem wi;
-            int stage = 0, local = 0;
+            int stage = 0;
             uint32_t phase = 0;
-            bool ok = true;
-            for (int n = 0; ok && sch.get(p, n, wi); ++n) {
-                const int k0 = wi.k0, k1 = wi.k1;
-                const int acc = local % C::NACC;
-                const uint32_t aph = (local / C::NACC) & 1u;
-                ++local;
-                if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, p.status, GK_DEV_TIMEOUT_MMA,
-                               tmo)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d = tmem_base + static_cast<uint32_t>(acc * NB);
-                for (int kb = k0; kb < k1; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, abort_flag, p.status, GK_DEV_TIMEOUT_MMA,
-                                   tmo)) {
+            if (!p.sk) {
+                // item by item, the items taking turns on the accumulators (plain loops: this
+                // thread's per-stage turnaround is on the streaming's critical path)
+                GemvItem wi;
+                int local = 0;
+                bool ok = true;
+                for (int n = 0; ok && sch.get(p, n, wi); ++n) {
+                    const int k0 = wi.k0, k1 = wi.k1;
+                    const int acc = local % C::NACC;
+                    const uint32_t aph = (local / C::NACC) & 1u;
+                    ++local;
+                    if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, p.status,
+                                   GK_DEV_TIMEOUT_MMA, tmo)) {
                         ok = false;
                         break;
                     }
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + static_cast<uint32_t>(acc * NB);
+                    for (int kb = k0; kb < k1; ++kb) {
+                        if (!mbar_wait(&full[stage], phase, abort_flag, p.status,
+                                       GK_DEV_TIMEOUT_MMA, tmo)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a0 = smem_u32(sW + stage * C::W_BYTES);
+                        const uint32_t b0 = smem_u32(sX + stage * C::X_BYTES);
+#pragma unroll
+                        for (int ks = 0; ks < BKB / MMA_KB; ++ks) {
+                            const uint64_t ad = sdesc_kmajor_sw128(a0 + ks * MMA_KB);
+                            const uint64_t bd = sdesc_kmajor_sw128(b0 + ks * MMA_KB);
+                            const uint32_t accum = (kb != k0 || ks != 0) ? 1u : 0u;
+                            if constexpr (KIND == Kind::I8)
+                                mma_i8(d, ad, bd, idesc, accum);
+                            else
+                                mma_f16(d, ad, bd, idesc, accum);
+                        }
+                        mma_commit(&empty[stage]);
+                        if (++stage == nst) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    mma_commit(&tfull[acc]);
+                }
+            } else {
+                // stream-K: K block by K block, every item in its own accumulator (item order:
+                // writer, whole tiles, finisher; the planner keeps them within NACC)
+                int acc = 0;
+                auto mma_stage = [&](int kb, int k0, int k1) {
+                    const uint32_t d = tmem_base + static_cast<uint32_t>(acc * NB);
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.status, GK_DEV_TIMEOUT_MMA,
+                                   tmo))
+                        return false;
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(sW + stage * C::W_BYTES);
                     const uint32_t b0 = smem_u32(sX + stage * C::X_BYTES);
@@ -363,13 +507,34 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
                             mma_f16(d, ad, bd, idesc, accum);
                     }
                     mma_commit(&empty[stage]);
-                    if (++stage == STAGES) {
+                    if (++stage == nst) {
                         stage = 0;
                         phase ^= 1u;
                     }
+                    if (kb == k1 - 1) mma_commit(&tfull[acc]);
+                    return true;
+                };
+                const int nitems = (sch.has_wr ? 1 : 0) + sch.w_cnt + (sch.has_fin ? 1 : 0);
+                bool ok = nitems <= C::NACC;
+                if (!ok) {
+                    *abort_flag = 1;
+                    atomicOr(p.status, GK_DEV_TIMEOUT_MMA);
                 }
-                if (!ok) break;
-                mma_commit(&tfull[acc]);
+                const int w0 = sch.has_wr ? 1 : 0;
+                for (int kb = 0; kb < p.num_kb && ok; ++kb) {
+                    if (sch.has_wr && kb >= sch.wr.k0 && kb < sch.wr.k1) {
+                        acc = 0;
+                        ok = mma_stage(kb, sch.wr.k0, sch.wr.k1);
+                    }
+                    for (int j = 0; j < sch.w_cnt && ok; ++j) {
+                        acc = w0 + j;
+                        ok = mma_stage(kb, 0, p.num_kb);
+                    }
+                    if (ok && sch.has_fin && kb >= sch.fin.k0) {
+                        acc = nitems - 1;
+                        ok = mma_stage(kb, sch.fin.k0, p.num_kb);
+                    }
+                }
             }
             // every MMA this CTA issued has finished before TMEM is released
             mma_commit(drain);
@@ -401,9 +566,11 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
         int local = 0;
         for (int n = 0; sch.get(p, n, wi); ++n) {
             const int tile = wi.tile;
-            const int acc = local % C::NACC;
-            const uint32_t aph = (local / C::NACC) & 1u;
+            // stream-K: item n's own accumulator, used once; otherwise the items take turns
+            const int acc = p.sk ? n : local % C::NACC;
+            const uint32_t aph = p.sk ? 0u : (local / C::NACC) & 1u;
             ++local;
+            if (p.sk && n >= C::NACC) break;
             grow = static_cast<int64_t>(tile) * BM + row;
             const bool row_ok = grow < p.Mk;
             // this row's requant constants, fetched while the MMAs run
@@ -420,6 +587,59 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
                 }
                 if (e.scale_axis != AX_N) make_scale_param(rs, r_se, r_nms, r_ulo, r_uhi);
                 r_bp = static_cast<uint32_t>(rb) + 0x80000000u;
+            }
+            // A finisher gathers the writers' partials of its 32 rows while its own last MMAs
+            // run: it waits (bounded) until the tile's writers have counted in, then sums their
+            // slots in slot order (exact for integers, a fixed order for floats).
+            uint32_t pre[NCH][CH];
+            if (wi.role == GEMV_FINISHER) {
+                uint32_t ok = 1;
+                if (lane == 0) {
+                    const volatile uint32_t* ctr = p.ctr + static_cast<int64_t>(tile) * 4 + q;
+                    const uint32_t want = (p.epoch << 8) | static_cast<uint32_t>(wi.nctr - 1);
+                    if (*ctr != want) {
+                        const uint64_t t0 = globaltimer_ns();
+                        while (*ctr != want) {
+                            if (*abort_flag || globaltimer_ns() - t0 > tmo) {
+                                if (!*abort_flag) {
+                                    *abort_flag = 1;
+                                    atomicOr(p.status, GK_DEV_TIMEOUT_EPILOGUE);
+                                }
+                                ok = 0;
+                                break;
+                            }
+                        }
+                    }
+                }
+                if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+                __threadfence();
+                const uint32_t* base = p.part +
+                                       static_cast<int64_t>(tile) * GEMV_SK_MAXC * (BM * NB) +
+                                       static_cast<int64_t>(row) * NB;
+#pragma unroll
+                for (int c = 0; c < NCH; ++c)
+#pragma unroll
+                    for (int i = 0; i < CH; ++i) pre[c][i] = 0u;
+                for (int j = 0; j + 1 < wi.nctr; ++j) {
+                    const uint4* src =
+                        reinterpret_cast<const uint4*>(base + static_cast<int64_t>(j) * (BM * NB));
+#pragma unroll
+                    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+                        for (int g = 0; g < CH / 4; ++g) {
+                            const uint4 x = __ldcg(src + (c * CH) / 4 + g);
+                            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) {
+                                uint32_t& d = pre[c][4 * g + t];
+                                if constexpr (KIND == Kind::I8)
+                                    d += xs[t];
+                                else
+                                    d = __float_as_uint(__fadd_rn(__uint_as_float(d),
+                                                                  __uint_as_float(xs[t])));
+                            }
+                        }
+                }
             }
             if (!warp_wait(&tfull[acc], aph, abort_flag, p.status, GK_DEV_TIMEOUT_EPILOGUE, tmo))
                 break;
@@ -438,13 +658,11 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
             if (lane == 0) mbar_arrive(&tempty[acc]);
             have = true;
             if (p.split > 1) break;  // one item; summed across the cluster below
-            if (wi.nctr > 1) {
-                // A shared tile: publish this CTA's partial rows in its slot, then count this
-                // warp's 32-row quarter; the last of the tile's CTAs to arrive sums the slots
-                // in slot order (exact for integers, a fixed order for floats) and finishes.
-                uint32_t* base = p.part + static_cast<int64_t>(tile) * GEMV_SK_MAXC * (BM * NB) +
+            if (wi.role == GEMV_WRITER) {
+                // publish this CTA's partial rows in its slot, then count this warp's quarter
+                uint32_t* mine = p.part + static_cast<int64_t>(tile) * GEMV_SK_MAXC * (BM * NB) +
+                                 static_cast<int64_t>(wi.slot) * (BM * NB) +
                                  static_cast<int64_t>(row) * NB;
-                uint32_t* mine = base + static_cast<int64_t>(wi.slot) * (BM * NB);
 #pragma unroll
                 for (int c = 0; c < NCH; ++c)
 #pragma unroll
@@ -453,7 +671,6 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
                                      v[c][4 * g + 2], v[c][4 * g + 3]);
                 __threadfence();
                 __syncwarp();
-                uint32_t last = 0;
                 if (lane == 0) {
                     uint32_t* ctr = p.ctr + static_cast<int64_t>(tile) * 4 + q;
                     uint32_t old = atomicAdd(ctr, 0u);
@@ -461,40 +678,23 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
                         const uint32_t nv =
                             (old >> 8) == p.epoch ? old + 1u : ((p.epoch << 8) | 1u);
                         const uint32_t prev = atomicCAS(ctr, old, nv);
-                        if (prev == old) {
-                            last = (nv & 0xFFu) == static_cast<uint32_t>(wi.nctr) ? 1u : 0u;
-                            break;
-                        }
+                        if (prev == old) break;
                         old = prev;
                     }
                 }
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (!last) continue;
-                __threadfence();
+                continue;
+            }
+            if (wi.role == GEMV_FINISHER) {
 #pragma unroll
                 for (int c = 0; c < NCH; ++c)
 #pragma unroll
-                    for (int i = 0; i < CH; ++i) v[c][i] = 0u;
-                for (int j = 0; j < wi.nctr; ++j) {
-                    const uint4* src = reinterpret_cast<const uint4*>(
-                        base + static_cast<int64_t>(j) * (BM * NB));
-#pragma unroll
-                    for (int c = 0; c < NCH; ++c)
-#pragma unroll
-                        for (int g = 0; g < CH / 4; ++g) {
-                            const uint4 x = __ldcg(src + (c * CH) / 4 + g);
-                            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                            for (int t = 0; t < 4; ++t) {
-                                uint32_t& d = v[c][4 * g + t];
-                                if constexpr (KIND == Kind::I8)
-                                    d += xs[t];
-                                else
-                                    d = __float_as_uint(__fadd_rn(__uint_as_float(d),
-                                                                  __uint_as_float(xs[t])));
-                            }
-                        }
-                }
+                    for (int i = 0; i < CH; ++i) {
+                        if constexpr (KIND == Kind::I8)
+                            v[c][i] += pre[c][i];
+                        else
+                            v[c][i] = __float_as_uint(
+                                __fadd_rn(__uint_as_float(pre[c][i]), __uint_as_float(v[c][i])));
+                    }
             }
             int qm = QM_GENERAL;
             if constexpr (QUANT) qm = pick_quant_mode(e, r_se);
@@ -722,9 +922,10 @@ bool plan_gemv(const TcProblem& p, TcPlan* plan, bool allow_sk) {
     // Whole tiles once about three quarters of the SMs have one; else cut K inside clusters
     // of up to 8 (portable cluster size) so that tiles * split approaches the SM count.
     int split = 1;
+    const int max_split = p.gemv_split > 0 ? p.gemv_split : 8;
     if (static_cast<int64_t>(pl.tiles_m) * 4 < static_cast<int64_t>(sms) * 3) {
         split = sms / pl.tiles_m;
-        if (split > 8) split = 8;
+        if (split > max_split) split = max_split;
         if (split > pl.num_kb) split = pl.num_kb;
         if (split < 1) split = 1;
     }
@@ -735,8 +936,9 @@ bool plan_gemv(const TcProblem& p, TcPlan* plan, bool allow_sk) {
     // K blocks (so at most GEMV_SK_MAXC CTAs share a tile): the bytes each SM streams, which
     // bound a call, are then the same on every SM.
     const int64_t units = static_cast<int64_t>(pl.tiles_m) * pl.num_kb;
+    // (a run of at most 2*num_kb + 1 units touches at most four tiles: one accumulator each)
     if (allow_sk && split == 1 && pl.num_kb >= 2 && pl.tiles_m % sms != 0 &&
-        units / sms >= (pl.num_kb + 1) / 2) {
+        units / sms >= (pl.num_kb + 1) / 2 && units / sms <= 2 * pl.num_kb) {
         pl.gemv_sk = 1;
         pl.grid = sms;
         pl.sk_iters = units;
@@ -758,6 +960,7 @@ int launch_gemv(const TcProblem& pr, const TcPlan& plan, char* err, size_t errle
     gp.tiles = plan.tiles_m;
     gp.early_weights = plan.pdl;
     gp.timeout_ns = 4000000000ull;
+    gp.stages = pr.stages;
     gp.status = device_status_ptr();
     gp.e = pr.e;
     if (pr.kind == Kind::I8) {

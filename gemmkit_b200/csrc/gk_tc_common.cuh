@@ -504,6 +504,12 @@ __device__ __forceinline__ void epilogue_chunk_mirrored_wide(const uint32_t (&v)
 // Host helpers shared by the launchers (gk_tc_gemm.cu).
 int encode_operand(CUtensorMap* map, const Operand& op, int64_t K, int64_t batch, int es,
                    int box_rows, char* err, size_t errlen);
+// Tensor map for TMA stores of a byte output: element (e, i, j) at out + e*obs + i*ldo + j,
+// cols x rows x batch, box box_cols x box_rows x 1 with the swizzle of its box_cols-byte rows
+// (32, 64 or 128).
+int encode_output_u8(CUtensorMap* map, void* out, int64_t cols, int64_t rows, int64_t batch,
+                     int64_t ldo, int64_t obs, int box_cols, int box_rows, char* err,
+                     size_t errlen);
 // Tensor map over the tiled prepacked layout (Operand::slab): 128-byte rows already in
 // swizzled order, so the map itself does not swizzle; box = box_rows rows of one K block.
 int encode_tiled_operand(CUtensorMap* map, const Operand& op, int64_t K, int box_rows, char* err,

@@ -66,6 +66,8 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                    const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
     using C = TileCfg<OUT, BN>;
     constexpr int STAGES = C::STAGES;
+    // ring depth in use: the run-time cap (GEMMKIT_CUDA_STAGES) or the whole ring
+    const int nst = (p.stages > 0 && p.stages < STAGES) ? p.stages : STAGES;
     constexpr int CH = C::CH;
     constexpr int NCH = C::NCH;
     constexpr int NEPI_T = 32 * C::NEPI;  // epilogue threads
@@ -156,7 +158,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                                     tn * BN, zb);
                     issued |= 1u << stage;
                     last_par = (last_par & ~(1u << stage)) | (phase << stage);
-                    if (++stage == STAGES) {
+                    if (++stage == nst) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -215,7 +217,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                             mma_f16(d, ad, bd, idesc, accum);
                     }
                     mma_commit(&empty[stage]);
-                    if (++stage == STAGES) {
+                    if (++stage == nst) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -550,6 +552,54 @@ int encode_operand(CUtensorMap* map, const Operand& op, int64_t K, int64_t batch
     return 0;
 }
 
+int encode_output_u8(CUtensorMap* map, void* out, int64_t cols, int64_t rows, int64_t batch,
+                     int64_t ldo, int64_t obs, int box_cols, int box_rows, char* err,
+                     size_t errlen) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    // cached with the operand maps; a negative element size marks an output map
+    const TmapKey key{out, cols, rows, ldo, batch > 1 ? obs : 0, batch, -box_cols, box_rows};
+    for (int i = 0; i < g_tmap_used; ++i)
+        if (g_tmap_cache[i].dev == dev && g_tmap_cache[i].key == key) {
+            *map = g_tmap_cache[i].map;
+            return 0;
+        }
+    PFN_tmapEncodeTiled enc = get_encode();
+    if (!enc) {
+        snprintf(err, errlen, "gemmkit: cuTensorMapEncodeTiled is unavailable (driver too old?)");
+        return 5;
+    }
+    if ((reinterpret_cast<uintptr_t>(out) & 15) || (ldo & 15) || ldo <= 0 ||
+        (batch > 1 && (obs & 15)) || (box_cols != 32 && box_cols != 64 && box_cols != 128)) {
+        snprintf(err, errlen, "gemmkit: internal error: output not TMA-aligned");
+        return 1;
+    }
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                          static_cast<cuuint64_t>(batch > 1 ? batch : 1)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(ldo),
+                             static_cast<cuuint64_t>(batch > 1 ? obs : ldo * rows)};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapSwizzle sw = box_cols == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
+                                  : box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                   : CU_TENSOR_MAP_SWIZZLE_128B;
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, out, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        snprintf(err, errlen, "gemmkit: cuTensorMapEncodeTiled (output) failed (%d)",
+                 static_cast<int>(r));
+        return 3;
+    }
+    TmapEntry& e = g_tmap_cache[g_tmap_next];
+    e.key = key;
+    e.map = *map;
+    e.dev = dev;
+    g_tmap_next = (g_tmap_next + 1) % TMAP_CACHE;
+    if (g_tmap_used < TMAP_CACHE) ++g_tmap_used;
+    return 0;
+}
+
 int encode_tiled_operand(CUtensorMap* map, const Operand& op, int64_t K, int box_rows, char* err,
                          size_t errlen) {
     PFN_tmapEncodeTiled enc = get_encode();
@@ -783,6 +833,7 @@ int launch_tc_gemm_planned(const TcProblem& pr, const TcPlan& plan, char* err, s
     gp.b_batched = pr.b.bs != 0 && pr.batch > 1;
     gp.timeout_ns = 4000000000ull;
     gp.status = device_status_ptr();
+    gp.stages = pr.stages;
     gp.e = pr.e;
     if (plan.gemv) return launch_gemv(pr, plan, err, errlen);
     if (plan.pair) return launch_pair(pr, plan, gp, err, errlen);

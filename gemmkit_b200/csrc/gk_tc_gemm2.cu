@@ -41,7 +41,10 @@ namespace gk {
 template <Out OUT, int BN, bool EPI16 = false>
 struct PairCfg {
     static constexpr int NEPI = EPI16 ? 16 : 8;     // epilogue warps per CTA
-    static constexpr int THREADS = 64 + 32 * NEPI;
+    // the 16-warp form has a parameter warp (warp 2) that prepares each item's row and column
+    // parameters for the epilogue warps, which then start at warp 3
+    static constexpr int EPI_W0 = EPI16 ? 3 : 2;
+    static constexpr int THREADS = 32 * EPI_W0 + 32 * NEPI;
     static constexpr int NGROUPS = NEPI / 4;        // column groups (4 TMEM lane quarters each)
     static constexpr int WCOLS = BN / NGROUPS;      // accumulator columns per epilogue warp
     static constexpr int CH = EPI16 ? 16 : 32;
@@ -55,14 +58,40 @@ struct PairCfg {
     // 4-byte outputs keep a 4 KB tile per epilogue warp for mirrored (peer) stores
     static constexpr bool WIDE = (OUT == Out::I32 || OUT == Out::F32);
     static constexpr int EPI_STAGE_BYTES = WIDE ? NEPI * 32 * 32 * 4 : 0;
+    // The 16-warp form writes C through TMA stores: each warp stages its 32 x WCOLS output
+    // block in shared memory (two buffers, so one store drains while the next block fills).
+    static constexpr int STORE_BLOCK = 32 * WCOLS;
+    static constexpr int STORE_BYTES = EPI16 ? NEPI * 2 * STORE_BLOCK : 0;
     static constexpr int RAW_STAGES =
-        (SMEM_LIMIT - 1024 - BAR_BYTES - CP_BYTES - EPI_STAGE_BYTES) / STAGE_BYTES;
+        (SMEM_LIMIT - 1024 - STORE_BYTES - BAR_BYTES - CP_BYTES - EPI_STAGE_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = RAW_STAGES > 10 ? 10 : RAW_STAGES;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES + CP_BYTES + EPI_STAGE_BYTES;
+    // layout after the 1024-byte alignment: stages | store blocks | barriers | params | epi
+    static constexpr int OFF_STORE = STAGES * STAGE_BYTES;
+    static constexpr int OFF_BARS = OFF_STORE + STORE_BYTES;
+    static constexpr int OFF_CP = OFF_BARS + BAR_BYTES;
+    static constexpr int OFF_EPI = OFF_CP + CP_BYTES;
+    static constexpr int SMEM = 1024 + OFF_EPI + EPI_STAGE_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static_assert(BN == 128 || BN == 256, "pair tile width");
+    static_assert(!EPI16 || WCOLS == 64, "the store blocks use the 64-byte swizzle");
+    static_assert(OFF_STORE % 1024 == 0 && STORE_BLOCK % 1024 == 0, "store block alignment");
     static_assert(STAGES >= 2 && SMEM <= SMEM_LIMIT, "shared memory budget");
-    static_assert(2 * STAGES + 7 <= BAR_BYTES / 8 - 1, "barrier area");
+    static_assert(2 * STAGES + 10 <= BAR_BYTES / 8, "barrier area");
+    // The parameter warp's buffers (16-warp form, two items): per row {se, nms}, bias + 2^31
+    // and clamp; per column bias + 2^31; the item's position and each lane quarter's path.
+    static constexpr int PB_ROWSE = 0;                    // double2[BM]
+    static constexpr int PB_ROWBP = PB_ROWSE + BM * 16;   // uint32_t[BM]
+    static constexpr int PB_CLAMP = PB_ROWBP + BM * 4;    // uint2[BM]
+    static constexpr int PB_COLB = PB_CLAMP + BM * 8;     // uint32_t[BN]
+    static constexpr int PB_POS = PB_COLB + BN * 4;       // ItemPar
+    static constexpr int PB_BYTES = (PB_POS + 64 + 127) / 128 * 128;
+    static_assert(!EPI16 || 2 * PB_BYTES <= CP_BYTES, "parameter buffers");
+};
+
+// The position and per-quarter requantize path of an item (16-warp form's parameter buffer).
+struct ItemPar {
+    int b, tm, tn, c0, width;
+    int qmode[4];
 };
 
 // Item t of the pair schedule: its tile, its first column inside the tile and its width.
@@ -81,12 +110,101 @@ __device__ __forceinline__ void pair_item(int t, const GemmParams& p, int& tile,
     }
 }
 
+// The requantize loop of one warp's share of an item when every choice is settled before it:
+// a per-row or per-tensor scale (se / nms, and the clamp ulo / uhi on the general path), the
+// bias per column from the warp's shared-memory slice (BCOL) or per row (r_bp), ReLU or not,
+// rows of C vector-aligned and no mirrors. Each chunk is one TMEM load, the exact requantize,
+// saturating packs and 16-byte stores; of the warp's columns only the first ncol exist in C
+// (a chunk that C cuts is stored byte by byte). The warp hands the accumulator back after its
+// last TMEM load.
+// With TMA (the 16-warp form, whole items) the chunks go instead into the warp's shared-memory
+// store block sblk (32 rows of 64 bytes in the 64-byte swizzle: 16-byte piece j of row r at
+// piece j ^ ((r >> 1) & 3), conflict-free) and one TMA tensor store of the block at (x, y, z)
+// of tmC writes it to C; the store clips rows and columns past C. The caller has made sure the
+// store that last read sblk is done.
+template <bool SMALL, bool BCOL, bool RELU, bool U8, int CH, int NCH, bool TMA = false>
+__device__ __forceinline__ void quant_rows_fast(uint32_t tbase, int nch, int64_t ncol,
+                                                uint8_t* dst, bool row_ok, uint32_t bslice,
+                                                double se, double nms, double magic,
+                                                uint32_t r_bp, uint32_t ulo, uint32_t uhi, int zp,
+                                                int lo, uint32_t tempty_caddr, int lane,
+                                                uint8_t* sblk = nullptr,
+                                                const CUtensorMap* tmC = nullptr, int x = 0,
+                                                int y = 0, int z = 0) {
+    // 32-column chunks (8 epilogue warps) keep the next chunk's TMEM load in flight; 16-column
+    // chunks (16 warps, 96 registers) load one chunk at a time and rely on the other warps.
+    constexpr bool DB = CH == 32;
+    uint32_t va[32], vb[32];
+    tmem_ld_chunk<CH>(tbase, va);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        if (c >= nch) break;
+        uint32_t(&cur)[32] = (DB && (c & 1)) ? vb : va;
+        uint32_t(&nxt)[32] = (DB && (c & 1)) ? va : vb;
+        tmem_wait_ld();
+        reg_fence<CH>(cur);
+        if (c + 1 < nch) {
+            if constexpr (DB) tmem_ld_chunk<CH>(tbase + (c + 1) * CH, nxt);
+        } else {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster_relaxed(tempty_caddr);
+        }
+        uint32_t w[CH / 4];
+#pragma unroll
+        for (int g = 0; g < CH / 4; ++g) {
+            uint4 bq = make_uint4(r_bp, r_bp, r_bp, r_bp);
+            if constexpr (BCOL) bq = ld_shared_v4(bslice + static_cast<uint32_t>(c * CH + 4 * g) * 4u);
+            const uint32_t bs[4] = {bq.x, bq.y, bq.z, bq.w};
+            int qv[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                if constexpr (SMALL)
+                    qv[t] = requant_q_small(cur[4 * g + t], bs[t], se, nms, magic);
+                else
+                    qv[t] = requant_q(cur[4 * g + t], bs[t], se, nms, ulo, uhi, zp);
+                if constexpr (RELU) qv[t] = max(qv[t], lo);
+            }
+            w[g] = pack4_sat<U8>(qv[0], qv[1], qv[2], qv[3]);
+        }
+        if constexpr (TMA) {
+            static_assert(CH == 16, "one 16-byte piece per chunk and row");
+            *reinterpret_cast<uint4*>(sblk + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+        } else if (row_ok) {
+            if (c * CH + CH <= ncol) {
+#pragma unroll
+                for (int k = 0; k < CH / 16; ++k)
+                    st_global_v4(dst + c * CH + 16 * k, w[4 * k], w[4 * k + 1], w[4 * k + 2],
+                                 w[4 * k + 3]);
+            } else {
+                for (int i = 0; i < CH && c * CH + i < ncol; ++i)
+                    dst[c * CH + i] = static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3)));
+            }
+        }
+        if constexpr (!DB) {
+            if (c + 1 < nch) tmem_ld_chunk<CH>(tbase + (c + 1) * CH, va);
+        }
+    }
+    if constexpr (TMA) {
+        fence_proxy_async_smem();  // the block's bytes, before the async proxy reads them
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_3d(tmC, sblk, x, y, z);
+            bulk_commit_group();
+        }
+    }
+}
+
 template <Kind KIND, Out OUT, int BN, bool EPI16 = false>
 __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
     using C = PairCfg<OUT, BN, EPI16>;
     constexpr int STAGES = C::STAGES;
+    // ring depth in use: the run-time cap (GEMMKIT_CUDA_STAGES) or the whole ring
+    const int nst = (p.stages > 0 && p.stages < STAGES) ? p.stages : STAGES;
     constexpr int CH = C::CH;
     constexpr int NCH = C::NCH;
     constexpr int NEPI_T = 32 * C::NEPI;
@@ -98,19 +216,20 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
                                                ~static_cast<uintptr_t>(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * C::A_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+    uint8_t* sstore = smem + C::OFF_STORE;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BARS);
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
     uint64_t* tfull = bars + 2 * STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* pready = tfull + 4;
-    uint64_t* drain = tfull + 6;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 7);
+    uint64_t* pfree = tfull + 6;
+    uint64_t* drain = tfull + 8;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 9);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    ColParam* cparams = reinterpret_cast<ColParam*>(smem + STAGES * C::STAGE_BYTES + C::BAR_BYTES);
+    ColParam* cparams = reinterpret_cast<ColParam*>(smem + C::OFF_CP);
     uint32_t* cbias = reinterpret_cast<uint32_t*>(cparams + 2 * BN);
-    uint32_t* epi_stage = reinterpret_cast<uint32_t*>(smem + STAGES * C::STAGE_BYTES +
-                                                      C::BAR_BYTES + C::CP_BYTES);
+    uint32_t* epi_stage = reinterpret_cast<uint32_t*>(smem + C::OFF_EPI);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -129,7 +248,10 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], 2 * C::NEPI);  // every epilogue warp of both CTAs
-            mbar_init(&pready[a], NEPI_T);
+            // column params of the 8-warp form (every epilogue thread), or the parameter
+            // warp's item buffers of the 16-warp form (its 32 lanes; freed by the epilogue warps)
+            mbar_init(&pready[a], EPI16 ? 32 : NEPI_T);
+            mbar_init(&pfree[a], C::NEPI);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -197,7 +319,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
                         tma_load_3d_pair(sB + stage * C::B_BYTES, &tmB, fb, kb * BKE, brow, zb);
                     issued |= 1u << stage;
                     last_par = (last_par & ~(1u << stage)) | (phase << stage);
-                    if (++stage == STAGES) {
+                    if (++stage == nst) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -260,7 +382,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
                     }
                     mma_commit_pair(empty_own + 8u * stage);
                     mma_commit_pair(empty_peer + 8u * stage);
-                    if (++stage == STAGES) {
+                    if (++stage == nst) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -272,6 +394,177 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
             mma_commit_pair(drain_own);
             int dummy = 0;
             mbar_wait(drain, 0, &dummy, p.status, GK_DEV_TIMEOUT_DRAIN, tmo);
+        }
+    } else if (EPI16 && warp == 2) {
+        // ---------------- parameter warp (16-warp form) ----------------
+        // For each item, into parameter buffer (item parity): the item's position, each row's
+        // requantize constants and each column's bias, and the path of each 32-row quarter, so
+        // that the epilogue warps start on an item with a few shared-memory loads.
+        const EpiParams& e = p.e;
+        uint8_t* pbase = reinterpret_cast<uint8_t*>(cparams);
+        // The global loads of an item are issued one item ahead, into registers, so that their
+        // latency passes while the epilogue warps still work on the buffer being refilled.
+        struct Loads {
+            int b, tm, tn, c0, width;
+            float sc[4];
+            int32_t rb[4];
+            int32_t cb[BN / 32];
+        };
+        auto fetch = [&](int t, Loads& L) {
+            int tile;
+            pair_item<BN>(t, p, tile, L.c0, L.width);
+            decode_tile(tile, p, L.b, L.tm, L.tn);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {  // row lane + 32 j: lane quarter j
+                const int64_t grow =
+                    static_cast<int64_t>(L.tm) * 2 * BM + rank * BM + lane + 32 * j;
+                L.sc[j] = e.scale;
+                L.rb[j] = 0;
+                if (grow < p.Mk) {
+                    if (e.scale_axis == AX_M) L.sc[j] = e.scales[L.b * e.scale_bs + grow];
+                    if (e.bias_axis == AX_M) L.rb[j] = e.bias[L.b * e.bias_bs + grow];
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < BN / 32; ++i) {
+                const int c = lane + 32 * i;
+                const int64_t gc = static_cast<int64_t>(L.tn) * BN + L.c0 + c;
+                L.cb[i] = (e.bias_axis == AX_N && c < L.width && gc < p.Nk)
+                              ? e.bias[L.b * e.bias_bs + gc] : 0;
+            }
+        };
+        griddep_wait();  // parameters may belong to the previous kernel
+        Loads L;
+        if (pair < n_items) fetch(pair, L);
+        int local = 0;
+        for (int t = pair; t < n_items; t += npairs, ++local) {
+            const int buf = local & 1;
+            const uint32_t ph = (local >> 1) & 1;
+            if (!warp_wait(&pfree[buf], ph ^ 1u, abort_flag, p.status, GK_DEV_TIMEOUT_EPILOGUE,
+                           tmo))
+                break;
+            uint8_t* pb = pbase + buf * C::PB_BYTES;
+            double2* rowse = reinterpret_cast<double2*>(pb + C::PB_ROWSE);
+            uint32_t* rowbp = reinterpret_cast<uint32_t*>(pb + C::PB_ROWBP);
+            uint2* rowclamp = reinterpret_cast<uint2*>(pb + C::PB_CLAMP);
+            uint32_t* colb = reinterpret_cast<uint32_t*>(pb + C::PB_COLB);
+            ItemPar* ip = reinterpret_cast<ItemPar*>(pb + C::PB_POS);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int r = lane + 32 * j;
+                double se, nms;
+                make_scale_se(L.sc[j], se, nms);
+                rowse[r] = make_double2(se, nms);
+                rowbp[r] = static_cast<uint32_t>(L.rb[j]) + 0x80000000u;
+                const bool small = __all_sync(0xffffffffu, se <= 0x1p-9);
+                int qm = QM_GENERAL;
+                if (small && (e.zp & 1) == 0)
+                    qm = e.bias_axis == AX_N ? QM_SMALL_COLB : QM_SMALL_ROWB;
+                if (qm == QM_GENERAL) {
+                    uint32_t lo, hi;
+                    make_scale_clamp(se, lo, hi);
+                    rowclamp[r] = make_uint2(lo, hi);
+                }
+                if (lane == 0) ip->qmode[j] = qm;
+            }
+#pragma unroll
+            for (int i = 0; i < BN / 32; ++i)
+                colb[lane + 32 * i] = static_cast<uint32_t>(L.cb[i]) + 0x80000000u;
+            if (lane == 0) {
+                ip->b = L.b;
+                ip->tm = L.tm;
+                ip->tn = L.tn;
+                ip->c0 = L.c0;
+                ip->width = L.width;
+            }
+            __syncwarp();
+            mbar_arrive(&pready[buf]);  // every lane: its own writes are released
+            if (t + npairs < n_items) fetch(t + npairs, L);
+        }
+    } else if constexpr (EPI16) {
+        // ---------------- epilogue (16-warp form: warps 3 .. 18, both CTAs) ----------------
+        const int ew = warp - C::EPI_W0;  // 0 .. NEPI - 1
+        const int q = warp & 3;           // TMEM lane quarter (warp id mod 4)
+        const int cgroup = ew >> 2;       // column group of the item
+        const int row = q * 32 + lane;
+        const EpiParams& e = p.e;
+        const bool bcol = e.bias_axis == AX_N;
+        const bool relu = e.relu != 0;
+        const double magic = 6755399441055744.0 + static_cast<double>(e.zp);
+        constexpr bool U8 = OUT == Out::U8;
+        const uint8_t* pbase = reinterpret_cast<const uint8_t*>(cparams);
+        griddep_wait();  // outputs may belong to the previous kernel
+        int local = 0;
+        for (int t = pair; t < n_items; t += npairs, ++local) {
+            const int buf = local & 1;
+            const uint32_t ph = (local >> 1) & 1;
+            const int acc = buf;
+            if (!warp_wait(&pready[buf], ph, abort_flag, p.status, GK_DEV_TIMEOUT_EPILOGUE, tmo))
+                break;
+            const uint8_t* pb = pbase + buf * C::PB_BYTES;
+            const ItemPar* ip = reinterpret_cast<const ItemPar*>(pb + C::PB_POS);
+            const int b = ip->b, tm = ip->tm, tn = ip->tn, c0 = ip->c0, width = ip->width;
+            const int qm = ip->qmode[q];
+            const double2 sn = reinterpret_cast<const double2*>(pb + C::PB_ROWSE)[row];
+            const uint32_t r_bp = reinterpret_cast<const uint32_t*>(pb + C::PB_ROWBP)[row];
+            uint32_t r_ulo = 0, r_uhi = 0;
+            if (qm == QM_GENERAL) {
+                const uint2 cl = reinterpret_cast<const uint2*>(pb + C::PB_CLAMP)[row];
+                r_ulo = cl.x;
+                r_uhi = cl.y;
+            }
+            const int wcols = width / C::NGROUPS;
+            const int col_base = cgroup * wcols;
+            const int nch = wcols / CH;
+            const int64_t grow = static_cast<int64_t>(tm) * 2 * BM + rank * BM + row;
+            const bool row_ok = grow < p.Mk;
+            const int64_t gcol0 = static_cast<int64_t>(tn) * BN + c0;
+            const uint32_t bslice = smem_u32(pb + C::PB_COLB) + static_cast<uint32_t>(col_base) * 4u;
+            uint8_t* dst = static_cast<uint8_t*>(e.out) + static_cast<int64_t>(b) * e.obs +
+                           grow * e.ldo + gcol0 + col_base;
+            const bool tma = wcols == C::WCOLS;
+            uint8_t* sblk = sstore + (ew * 2 + buf) * C::STORE_BLOCK;
+            if (tma) {
+                if (lane == 0) bulk_wait_group_read<1>();  // the store of two items ago
+                __syncwarp();
+            }
+            const int ty = tm * 2 * BM + static_cast<int>(rank) * BM + q * 32;
+            if (!warp_wait(&tfull[acc], ph, abort_flag, p.status, GK_DEV_TIMEOUT_EPILOGUE, tmo))
+                break;
+            tc_fence_after();
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN + col_base);
+            auto run = [&](auto small_tag, auto bcol_tag, auto relu_tag) {
+                constexpr bool SM = decltype(small_tag)::value;
+                constexpr bool BC = decltype(bcol_tag)::value;
+                constexpr bool RL = decltype(relu_tag)::value;
+                if (tma)
+                    quant_rows_fast<SM, BC, RL, U8, CH, NCH, true>(
+                        tbase, nch, p.Nk - (gcol0 + col_base), dst, row_ok, bslice, sn.x, sn.y,
+                        magic, r_bp, r_ulo, r_uhi, e.zp, e.lo, tempty_l + 8u * acc, lane, sblk,
+                        &tmC, static_cast<int>(gcol0 + col_base), ty, b);
+                else
+                    quant_rows_fast<SM, BC, RL, U8, CH, NCH>(
+                        tbase, nch, p.Nk - (gcol0 + col_base), dst, row_ok, bslice, sn.x, sn.y,
+                        magic, r_bp, r_ulo, r_uhi, e.zp, e.lo, tempty_l + 8u * acc, lane);
+            };
+            using T = std::true_type;
+            using F = std::false_type;
+            if (qm != QM_GENERAL) {
+                if (bcol) {
+                    if (relu) run(T{}, T{}, T{}); else run(T{}, T{}, F{});
+                } else {
+                    if (relu) run(T{}, F{}, T{}); else run(T{}, F{}, F{});
+                }
+            } else {
+                if (bcol) {
+                    if (relu) run(F{}, T{}, T{}); else run(F{}, T{}, F{});
+                } else {
+                    if (relu) run(F{}, F{}, T{}); else run(F{}, F{}, F{});
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&pfree[buf]);  // this item's parameters are read
         }
     } else {
         // ---------------- epilogue (warps 2 .. 1 + NEPI, both CTAs) ----------------
@@ -414,6 +707,63 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
                 qm = pick_quant_mode(e, r_se);
                 if (qm == QM_GENERAL && e.scale_axis != AX_N) make_scale_clamp(r_se, r_ulo, r_uhi);
             }
+            // the straight-line loop covers every item of the 16-warp form (the host launches
+            // that form only for such problems), and the common layouts of the 8-warp form
+            bool fast = false;
+            if constexpr (C::QUANT) fast = EPI16 || (!col_params && e.vec && e.nmirror == 0);
+            if constexpr (C::QUANT) {
+                if (fast) {
+                    uint8_t* dst = static_cast<uint8_t*>(e.out) + obase + gcol0 + col_base;
+                    const uint32_t bslice = smem_u32(wslice);
+                    const double magic = 6755399441055744.0 + static_cast<double>(e.zp);
+                    constexpr bool U8 = OUT == Out::U8;
+                    // 16-warp form, whole item: the warp's block goes out through a TMA store
+                    // from its store block of this item's parity (the store of two items ago
+                    // on that block has finished reading it)
+                    const bool tma = EPI16 && wcols == C::WCOLS;
+                    uint8_t* sblk = sstore + ((warp - 2) * 2 + (local & 1)) * C::STORE_BLOCK;
+                    if (EPI16 && tma) {
+                        if (lane == 0) bulk_wait_group_read<1>();
+                        __syncwarp();
+                    }
+                    const int ty = tm * 2 * BM + static_cast<int>(rank) * BM + q * 32;
+                    auto run = [&](auto small_tag, auto bcol_tag, auto relu_tag) {
+                        constexpr bool SM = decltype(small_tag)::value;
+                        constexpr bool BC = decltype(bcol_tag)::value;
+                        constexpr bool RL = decltype(relu_tag)::value;
+                        if constexpr (EPI16) {
+                            if (tma) {
+                                quant_rows_fast<SM, BC, RL, U8, CH, NCH, true>(
+                                    tbase, nch, p.Nk - (gcol0 + col_base), dst, row_ok, bslice,
+                                    r_se, r_nms, magic, r_bp, r_ulo, r_uhi, e.zp, e.lo,
+                                    tempty_l + 8u * acc, lane, sblk, &tmC,
+                                    static_cast<int>(gcol0 + col_base), ty, b);
+                                return;
+                            }
+                        }
+                        quant_rows_fast<SM, BC, RL, U8, CH, NCH>(
+                            tbase, nch, p.Nk - (gcol0 + col_base), dst, row_ok, bslice, r_se,
+                            r_nms, magic, r_bp, r_ulo, r_uhi, e.zp, e.lo, tempty_l + 8u * acc,
+                            lane);
+                    };
+                    using T = std::true_type;
+                    using F = std::false_type;
+                    const bool small = qm != QM_GENERAL;
+                    if (small) {
+                        if (warp_bias) {
+                            if (e.relu) run(T{}, T{}, T{}); else run(T{}, T{}, F{});
+                        } else {
+                            if (e.relu) run(T{}, F{}, T{}); else run(T{}, F{}, F{});
+                        }
+                    } else {
+                        if (warp_bias) {
+                            if (e.relu) run(F{}, T{}, T{}); else run(F{}, T{}, F{});
+                        } else {
+                            if (e.relu) run(F{}, F{}, T{}); else run(F{}, F{}, F{});
+                        }
+                    }
+                }
+            }
             auto chunks = [&](auto qm_tag) {
                 constexpr int QM = decltype(qm_tag)::value;
                 uint32_t va[32], vb[32];
@@ -447,13 +797,21 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
                                                     r_fb);
                 }
             };
-            with_quant_mode<C::QUANT>(qm, chunks);
+            if constexpr (!EPI16) {
+                if (!fast) with_quant_mode<C::QUANT>(qm, chunks);
+            } else {
+                (void)chunks;
+            }
             // (the next item is located again rather than kept live across the chunk loop)
             if (t_next < n_items) pos = locate(t_next);
             if (C::QUANT && t_next < n_items) commit(raw_next, pos, acc ^ 1);
         }
     }
 
+    // the epilogue's TMA stores complete before the CTA (and its shared memory) goes away
+    if constexpr (EPI16) {
+        if (warp >= 2 && lane == 0) bulk_wait_group_all();
+    }
     // mirrored outputs went to peer GPUs: make them visible system-wide before exiting
     if (p.e.nmirror > 0 && warp >= 2) __threadfence_system();
     tc_fence_before();
@@ -486,6 +844,14 @@ static int launch_pair_one(const TcProblem& pr, const TcPlan& plan, GemmParams g
     gp.b_tiled = pr.b.slab ? static_cast<const uint8_t*>(pr.b.ptr) : nullptr;
     gp.a_slab = pr.a.slab;
     gp.b_slab = pr.b.slab;
+    // the 16-warp form stores C through TMA (byte outputs, vector-aligned, no mirrors)
+    CUtensorMap tc;
+    memset(&tc, 0, sizeof(tc));
+    if constexpr (EPI16) {
+        rc = encode_output_u8(&tc, pr.e.out, pr.Nk, pr.Mk, pr.batch, pr.e.ldo, pr.e.obs,
+                              C::WCOLS, 32, err, errlen);
+        if (rc) return rc;
+    }
     auto kern = tc_gemm_pair_kernel<KIND, OUT, BN, EPI16>;
     static int attr_done[64] = {0};
     int dev = 0;
@@ -552,7 +918,7 @@ static int launch_pair_one(const TcProblem& pr, const TcPlan& plan, GemmParams g
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pr.pdl ? 2 : 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, gp);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, gp);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         snprintf(err, errlen, "gemmkit: pair kernel launch failed: %s", cudaGetErrorString(e));
@@ -563,12 +929,18 @@ static int launch_pair_one(const TcProblem& pr, const TcPlan& plan, GemmParams g
 
 int launch_pair(const TcProblem& pr, const TcPlan& plan, const GemmParams& gp, char* err,
                 size_t errlen) {
-#define GK_PAIR_CASE(K, O)                                                               \
-    if (pr.kind == K && pr.out == O)                                                     \
-        return plan.bn == 256 ? launch_pair_one<K, O, 256>(pr, plan, gp, err, errlen)    \
-                              : launch_pair_one<K, O, 128>(pr, plan, gp, err, errlen);
-    // quantized output with a one- or two-block K: the epilogue-bound form
-    if (pr.kind == Kind::I8 && plan.bn == 256 && plan.num_kb <= 2) {
+    // the planner runs the pair kernel with 256-wide tiles only
+    if (plan.bn != 256) {
+        snprintf(err, errlen, "gemmkit: internal error: pair kernel tile width %d", plan.bn);
+        return 1;
+    }
+#define GK_PAIR_CASE(K, O) \
+    if (pr.kind == K && pr.out == O) return launch_pair_one<K, O, 256>(pr, plan, gp, err, errlen);
+    // quantized output with a one- or two-block K: the epilogue-bound form, whose epilogue is
+    // only the straight-line requantize loop (per-row or per-tensor scale, vector-aligned C,
+    // no mirrors)
+    if (pr.epi16 && pr.kind == Kind::I8 && plan.bn == 256 && plan.num_kb <= 2 &&
+        pr.e.scale_axis != AX_N && pr.e.vec && pr.e.nmirror == 0) {
         if (pr.out == Out::Q8)
             return launch_pair_one<Kind::I8, Out::Q8, 256, true>(pr, plan, gp, err, errlen);
         if (pr.out == Out::U8)

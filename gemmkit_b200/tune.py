@@ -2,8 +2,9 @@
 ``export GEMMKIT_CUDA_*=...`` lines to source before running an application.
 
 This is gemmkit-tune's method (gemmkit-tune/src/main.rs:100-245, 1578-1608) applied to the
-device engine's knobs (tile width, CTA-pair kernel, small-M streaming kernel, programmatic
-dependent launch, stream-K tail):
+device engine's knobs (tile width per shape class, CTA-pair kernel, its 16-warp epilogue form,
+ring depth, stream-K tail, small-M streaming kernel with its even stream-K split and its
+cluster K split, programmatic dependent launch), each scored on the shape class it steers:
 
 * each knob is swept alone, every other knob at the value in effect; candidates are tried in a
   fixed order with the incumbent first;
@@ -193,6 +194,51 @@ class TileFamily:
         return geomean([measure(t, f, w) for f, w, _ in self.calls])
 
 
+class ShortKFamily:
+    """Products whose K is one or two 128-byte blocks, where the requantizing epilogue is the
+    kernel: a batched requantized GEMM of BASELINE config 4's element shape and one plain
+    requantized GEMM with K = 200. Rate in GB/s of algorithmic traffic."""
+
+    def __init__(self, quick: bool):
+        import torch
+
+        import gemmkit_b200 as gk
+        g = torch.Generator(device="cuda").manual_seed(13)
+        self.calls = []
+        B, m, n, k = (64 if quick else 256), 512, 512, 128
+        a = torch.randint(-128, 128, (B * m * k,), dtype=torch.int8, device="cuda", generator=g)
+        bT = torch.randint(-128, 128, (B * n * k,), dtype=torch.int8, device="cuda", generator=g)
+        bias = torch.randint(-2**15, 2**15 + 1, (B * m,), dtype=torch.int32, device="cuda",
+                             generator=g)
+        sc = (torch.rand(B * n, device="cuda", generator=g) * 9e-4 + 1e-4).float()
+        c = torch.empty(B * m * n, dtype=torch.uint8, device="cuda")
+        req = gk.Requantize(gk.RequantScale.PerCol(sc), 128, bias, gk.AXIS_ROW)
+        keep = (a, bT, bias, sc, c, req)
+
+        def bcall(keep=keep):
+            a, bT, _, _, c, req = keep
+            gk.gemm_i8_requant_batched(B, m, k, n, a.data_ptr(), k, 1, m * k, bT.data_ptr(), 1, k,
+                                       n * k, req, m, n, c.data_ptr(), 1, m, m * n, out_u8=True)
+        self.calls.append((bcall, B * (m * k + n * k + m * n + 4 * m + 4 * n) / 1e9, keep))
+        m2, k2, n2 = (2048, 200, 2048) if quick else (4096, 200, 4096)
+        a2 = torch.randint(-127, 128, (m2 * k2,), dtype=torch.int8, device="cuda", generator=g)
+        b2 = torch.randint(-127, 128, (n2 * k2,), dtype=torch.int8, device="cuda", generator=g)
+        sc2 = (torch.rand(n2, device="cuda", generator=g) * 9e-4 + 1e-4).float()
+        c2 = torch.empty(m2 * n2, dtype=torch.int8, device="cuda")
+        req2 = gk.Requantize(gk.RequantScale.PerCol(sc2), 0)
+        keep2 = (a2, b2, sc2, c2, req2)
+
+        def kcall(keep=keep2):
+            a2, b2, _, c2, req2 = keep
+            gk.gemm_i8_requant_ex_unchecked(m2, k2, n2, a2.data_ptr(), k2, 1, b2.data_ptr(), 1,
+                                            k2, req2, c2.data_ptr(), 1, m2)
+        self.calls.append((kcall, (m2 * k2 + n2 * k2 + m2 * n2 + 4 * n2) / 1e9, keep2))
+        self.unit = "GB/s"
+
+    def probe(self, t: Timing) -> Stat:
+        return geomean([measure(t, f, w) for f, w, _ in self.calls])
+
+
 class SmallMFamily:
     """Back-to-back requantized small-M calls over prepacked weights (BASELINE config 5 shapes),
     so launch overlap counts. Rate in GB/s of weight streaming."""
@@ -205,6 +251,20 @@ class SmallMFamily:
         k, n = 4096, (7168 if quick else 14336)
         self.calls = []
         sets = []
+        # a narrow weight matrix too (few 128-channel tiles: the cluster K split)
+        bTn = torch.randint(-127, 128, (2048 * k,), dtype=torch.int8, device="cuda", generator=g)
+        scn = (torch.rand(2048, device="cuda", generator=g) * 9e-4 + 1e-4).float()
+        narrow = (gk.prepack_rhs_i8(gk.MatRef.new(bTn, k, 2048, 1, k)), scn)
+        del bTn
+        an = torch.randint(-127, 128, (k,), dtype=torch.int8, device="cuda", generator=g)
+        cn = torch.empty(2048, dtype=torch.int8, device="cuda")
+        reqn = gk.Requantize(gk.RequantScale.PerCol(scn), 0)
+
+        def ncall(keep=(an, cn, narrow, reqn)):
+            an, cn, narrow, reqn = keep
+            gk.gemm_i8_packed_b_requant(1, an.data_ptr(), k, 1, narrow[0], reqn, cn.data_ptr(),
+                                        2048, 1)
+        self.calls.append((ncall, (k * 2048 + k + 2048 + 4 * 2048) / 1e9, (an, cn, narrow, reqn)))
         for _ in range(3):  # rotate weight sets so the stream does not sit in L2
             bT = torch.randint(-127, 128, (n * k,), dtype=torch.int8, device="cuda", generator=g)
             sc = (torch.rand(n, device="cuda", generator=g) * 9e-4 + 1e-4).float()
@@ -229,12 +289,19 @@ class SmallMFamily:
         return geomean([measure(t, f, w) for f, w, _ in self.calls])
 
 
-# knob -> (extra candidates, families it is scored on)
+# knob -> (extra candidates, families it is scored on). The families are gemmkit-tune's shape
+# classes for this engine: large tiles, short K (epilogue-bound) and small M (bandwidth-bound);
+# the tile width gets one entry per class (GEMMKIT_CUDA_BN, GEMMKIT_CUDA_BN_SHORTK).
 KNOBS = {
     "GEMMKIT_CUDA_BN": ([128, 192, 256], ("tile",)),
     "GEMMKIT_CUDA_PAIR": ([0, 1], ("tile",)),
     "GEMMKIT_CUDA_STREAMK": ([0, 1], ("tile",)),
+    "GEMMKIT_CUDA_STAGES": ([4, 6, 8], ("tile", "short_k")),
+    "GEMMKIT_CUDA_BN_SHORTK": ([128, 256], ("short_k",)),
+    "GEMMKIT_CUDA_EPI16": ([0, 1], ("short_k",)),
     "GEMMKIT_CUDA_GEMV": ([0, 1], ("small_m",)),
+    "GEMMKIT_CUDA_GEMV_SK": ([0, 1], ("small_m",)),
+    "GEMMKIT_CUDA_GEMV_SPLIT": ([2, 4, 8], ("small_m",)),
     "GEMMKIT_CUDA_PDL": ([0, 1], ("small_m", "tile")),
 }
 
@@ -263,6 +330,8 @@ def run(argv=None) -> tuple[list[KnobResult], str]:
     fams = {}
     if "tile" in need:
         fams["tile"] = TileFamily(args.quick)
+    if "short_k" in need:
+        fams["short_k"] = ShortKFamily(args.quick)
     if "small_m" in need:
         fams["small_m"] = SmallMFamily(args.quick)
 

@@ -236,7 +236,9 @@ def test_knobs_get_set_and_validation():
     import gemmkit_b200 as gk
     names = gk.knob_names()
     assert names == ["GEMMKIT_CUDA_BN", "GEMMKIT_CUDA_PAIR", "GEMMKIT_CUDA_GEMV",
-                     "GEMMKIT_CUDA_PDL", "GEMMKIT_CUDA_STREAMK", "GEMMKIT_CUDA_GEMV_SK"]
+                     "GEMMKIT_CUDA_PDL", "GEMMKIT_CUDA_STREAMK", "GEMMKIT_CUDA_GEMV_SK",
+                     "GEMMKIT_CUDA_BN_SHORTK", "GEMMKIT_CUDA_EPI16", "GEMMKIT_CUDA_STAGES",
+                     "GEMMKIT_CUDA_GEMV_SPLIT"]
     base = {n: gk.knob_get(n) for n in names}
     try:
         gk.knob_set("GEMMKIT_CUDA_BN", 128)
@@ -249,6 +251,15 @@ def test_knobs_get_set_and_validation():
             gk.knob_set("GEMMKIT_CUDA_PDL", 2)
         with pytest.raises(gk.GemmkitError, match="unknown knob"):
             gk.knob_set("GEMMKIT_CUDA_NOPE", 1)
+        gk.knob_set("GEMMKIT_CUDA_STAGES", 4)
+        assert gk.knob_get("GEMMKIT_CUDA_STAGES") == 4
+        with pytest.raises(gk.GemmkitError, match="cannot be 1"):
+            gk.knob_set("GEMMKIT_CUDA_STAGES", 1)
+        gk.knob_set("GEMMKIT_CUDA_GEMV_SPLIT", 8)
+        with pytest.raises(gk.GemmkitError, match="cannot be 9"):
+            gk.knob_set("GEMMKIT_CUDA_GEMV_SPLIT", 9)
+        gk.knob_set("GEMMKIT_CUDA_BN_SHORTK", 192)
+        assert gk.knob_get("GEMMKIT_CUDA_BN_SHORTK") == 192
     finally:
         for n in names:
             gk.knob_set(n, -1)  # drop the overrides
