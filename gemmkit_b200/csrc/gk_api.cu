@@ -94,16 +94,18 @@ int check_device(int* dev_out) {
 //   GEMMKIT_CUDA_STAGES   shared-memory ring depth cap of the kernels (0 = their whole ring,
 //                         else 2 .. 12)
 //   GEMMKIT_CUDA_GEMV_SPLIT largest cluster K split of the small-M kernel (0 = up to 8)
+//   GEMMKIT_CUDA_MN_B     1 = an N-contiguous i8 B is read MN-major by the tile kernel (no
+//                         transpose pack; tiles at most 128 wide); 0 = packed K-major first
 enum KnobId {
     K_BN = 0, K_PAIR, K_GEMV, K_PDL, K_STREAMK, K_GEMVSK, K_BNSHORTK, K_EPI16, K_STAGES,
-    K_GEMVSPLIT, K_COUNT
+    K_GEMVSPLIT, K_MNB, K_COUNT
 };
 const char* const kKnobEnv[K_COUNT] = {
     "GEMMKIT_CUDA_BN",       "GEMMKIT_CUDA_PAIR",      "GEMMKIT_CUDA_GEMV",
     "GEMMKIT_CUDA_PDL",      "GEMMKIT_CUDA_STREAMK",   "GEMMKIT_CUDA_GEMV_SK",
     "GEMMKIT_CUDA_BN_SHORTK", "GEMMKIT_CUDA_EPI16",    "GEMMKIT_CUDA_STAGES",
-    "GEMMKIT_CUDA_GEMV_SPLIT"};
-const int64_t kKnobDefault[K_COUNT] = {0, 1, 1, 1, 0, 0, 0, 1, 0, 0};
+    "GEMMKIT_CUDA_GEMV_SPLIT", "GEMMKIT_CUDA_MN_B"};
+const int64_t kKnobDefault[K_COUNT] = {0, 1, 1, 1, 0, 0, 0, 1, 0, 0, 1};
 std::atomic<int64_t> g_knob_set[K_COUNT];  // value + 1; 0 = no run-time override
 
 bool knob_valid(int id, int64_t v) {
@@ -147,6 +149,7 @@ bool pair_enabled() { return knob(K_PAIR) == 1; }
 bool gemv_enabled() { return knob(K_GEMV) == 1; }
 bool pdl_enabled() { return knob(K_PDL) == 1; }
 bool gemv_sk_enabled() { return knob(K_GEMVSK) == 1; }
+bool mn_major_enabled() { return knob(K_MNB) == 1; }
 
 int tile_n_override(int64_t k_bytes = -1) {
     if (g_tile_n >= 0) return g_tile_n;
@@ -553,6 +556,15 @@ int execute(const Job& j) {
     pr.stages = static_cast<int>(knob(K_STAGES));
     pr.epi16 = static_cast<int>(knob(K_EPI16));
     pr.gemv_split = static_cast<int>(knob(K_GEMVSPLIT));
+    // An N-contiguous i8 right-hand side (row-major B of C = A*B) is read MN-major by the
+    // tile kernel's TMA, with no transpose pack: rows contiguous, K at a 16-byte pitch.
+    if (need[1] && j.kind == gk::Kind::I8 && j.batch == 1 && kb.rs == 1 && kb.ks >= kb.rows &&
+        kb.ks % 16 == 0 && !(reinterpret_cast<uintptr_t>(kb.p) & 15) && Nk > 64 &&
+        (pr.bn == 0 || pr.bn >= 32) && pr.bn != 16 && mn_major_enabled()) {
+        need[1] = 0;
+        pr.b.mn_ld = kb.ks;
+        if (pr.bn == 192 || pr.bn == 256) pr.bn = 128;
+    }
     // the planners look at which operand is in the tiled prepacked layout; the operands
     // themselves are filled in below, once any packing has its scratch
     pr.a.slab = ka.slab;
@@ -589,7 +601,8 @@ int execute(const Job& j) {
         cur += need[i];
     }
     pr.a = gk::Operand{ka.p, ka.rows, ka.rs, ka.bs, ka.slab};
-    pr.b = gk::Operand{kb.p, kb.rows, kb.rs, kb.bs, kb.slab};
+    const int64_t mn_ld = pr.b.mn_ld;
+    pr.b = gk::Operand{kb.p, kb.rows, kb.rs, kb.bs, kb.slab, mn_ld};
     char err[512] = "";
     rc = gk::launch_tc_gemm_planned(pr, plan, err, sizeof(err));
     if (rc) return set_err(rc, "%s", err);
@@ -684,7 +697,7 @@ void gk_workspace_free(gk_workspace* ws) {
 const char* gk_knob_names(void) {
     return "GEMMKIT_CUDA_BN,GEMMKIT_CUDA_PAIR,GEMMKIT_CUDA_GEMV,GEMMKIT_CUDA_PDL,"
            "GEMMKIT_CUDA_STREAMK,GEMMKIT_CUDA_GEMV_SK,GEMMKIT_CUDA_BN_SHORTK,GEMMKIT_CUDA_EPI16,"
-           "GEMMKIT_CUDA_STAGES,GEMMKIT_CUDA_GEMV_SPLIT";
+           "GEMMKIT_CUDA_STAGES,GEMMKIT_CUDA_GEMV_SPLIT,GEMMKIT_CUDA_MN_B";
 }
 
 int gk_knob_get(const char* name, int64_t* value) {

@@ -69,6 +69,8 @@ struct GemmParams {
     const uint8_t* a_tiled;
     const uint8_t* b_tiled;
     int64_t a_slab, b_slab;  // bytes between consecutive 128-byte K blocks
+    // 1: B is read MN-major (its Nk rows contiguous, K at a pitch): tile kernel, i8, BN <= 128
+    int32_t b_mn;
     // Stream-K tail: tiles [0, dp_tiles) run whole, round-robin over the CTAs; the K blocks
     // of the remaining tiles are spread evenly over all CTAs. A tile cut between CTAs leaves
     // 32-bit partial accumulators in sk_part; the last CTA to finish a 32-row x WCOLS region
@@ -97,6 +99,9 @@ struct Operand {
     // (chunk j of row r stored at j ^ (r % 8)). Any 8-row-aligned run of rows of one block is
     // then a contiguous copy that lands in shared memory exactly as the MMA reads it.
     int64_t slab;
+    // mn_ld > 0: the operand is MN-major instead: element (r, p) at ptr + r + p*mn_ld (the
+    // rows contiguous, K at pitch mn_ld elements; an N-contiguous right-hand side, i8 only)
+    int64_t mn_ld;
 };
 
 struct TcProblem {

@@ -172,6 +172,22 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
     return d;
 }
 
+// Shared-memory matrix descriptor, MN-major operand written by a TMA box of `rowb`-byte rows
+// (32, 64 or 128 bytes of the MN dimension, swizzled with the same span): the swizzle atom is
+// 8 K-rows x rowb bytes, the next 8 K-rows follow at 8*rowb bytes (stride byte offset), and a
+// tile no wider than one atom needs no leading byte offset (set to 1). Layout field: 2 =
+// 128-byte, 4 = 64-byte, 6 = 32-byte swizzle.
+__device__ __forceinline__ uint64_t sdesc_mnmajor(uint32_t saddr, int rowb) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>(1u) << 16;
+    d |= static_cast<uint64_t>((8u * static_cast<uint32_t>(rowb)) >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    const uint64_t layout = rowb == 128 ? 2u : (rowb == 64 ? 4u : 6u);
+    d |= layout << 61;
+    return d;
+}
+
 // Instruction descriptors (32-bit): bits 4-5 accumulator format, 7-9 A format, 10-12 B
 // format, 15/16 A/B major (0 = K-major), 17-22 N >> 3, 24-28 M >> 4.
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {

@@ -510,6 +510,10 @@ int encode_operand(CUtensorMap* map, const Operand& op, int64_t K, int64_t batch
 int encode_output_u8(CUtensorMap* map, void* out, int64_t cols, int64_t rows, int64_t batch,
                      int64_t ldo, int64_t obs, int box_cols, int box_rows, char* err,
                      size_t errlen);
+// Tensor map over an MN-major i8 operand (Operand::mn_ld): box box_cols (32/64/128) of its
+// contiguous rows x 128 K-rows, swizzled by box_cols bytes.
+int encode_mn_operand(CUtensorMap* map, const Operand& op, int64_t K, int box_cols, char* err,
+                      size_t errlen);
 // Tensor map over the tiled prepacked layout (Operand::slab): 128-byte rows already in
 // swizzled order, so the map itself does not swizzle; box = box_rows rows of one K block.
 int encode_tiled_operand(CUtensorMap* map, const Operand& op, int64_t K, int box_rows, char* err,

@@ -153,6 +153,9 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                         bulk_load(sB + stage * C::B_BYTES,
                                   p.b_tiled + kb * p.b_slab + static_cast<int64_t>(tn) * BN * BKB,
                                   C::B_BYTES, &full[stage]);
+                    else if (p.b_mn)  // 128 K-rows x BN bytes of the N-contiguous B
+                        tma_load_3d(sB + stage * C::B_BYTES, &tmB, &full[stage], tn * BN,
+                                    kb * BKE, 0);
                     else
                         tma_load_3d(sB + stage * C::B_BYTES, &tmB, &full[stage], kb * BKE,
                                     tn * BN, zb);
@@ -181,6 +184,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
                 idesc = idesc_i8(BM, BN);
             else
                 idesc = idesc_f16(BM, BN, KIND == Kind::BF16);
+            if (p.b_mn) idesc |= 1u << 16;  // B is MN-major
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -209,7 +213,9 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
 #pragma unroll
                     for (int ks = 0; ks < BKB / MMA_KB; ++ks) {
                         const uint64_t ad = sdesc_kmajor_sw128(a0 + ks * MMA_KB);
-                        const uint64_t bd = sdesc_kmajor_sw128(b0 + ks * MMA_KB);
+                        // MN-major B: each MMA reads the next 32 K-rows of BN bytes
+                        const uint64_t bd = p.b_mn ? sdesc_mnmajor(b0 + ks * MMA_KB * BN, BN)
+                                                   : sdesc_kmajor_sw128(b0 + ks * MMA_KB);
                         const uint32_t accum = (kb != w.k0 || ks != 0) ? 1u : 0u;
                         if constexpr (KIND == Kind::I8)
                             mma_i8(d, ad, bd, idesc, accum);
@@ -600,6 +606,51 @@ int encode_output_u8(CUtensorMap* map, void* out, int64_t cols, int64_t rows, in
     return 0;
 }
 
+int encode_mn_operand(CUtensorMap* map, const Operand& op, int64_t K, int box_cols, char* err,
+                      size_t errlen) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    // cached with the operand maps; element size -1000 - box_cols marks an MN-major map
+    const TmapKey key{op.ptr, K, op.rows, op.mn_ld, 0, 1, -1000 - box_cols, 128};
+    for (int i = 0; i < g_tmap_used; ++i)
+        if (g_tmap_cache[i].dev == dev && g_tmap_cache[i].key == key) {
+            *map = g_tmap_cache[i].map;
+            return 0;
+        }
+    PFN_tmapEncodeTiled enc = get_encode();
+    if (!enc) {
+        snprintf(err, errlen, "gemmkit: cuTensorMapEncodeTiled is unavailable (driver too old?)");
+        return 5;
+    }
+    if ((reinterpret_cast<uintptr_t>(op.ptr) & 15) || (op.mn_ld & 15) || op.mn_ld < op.rows) {
+        snprintf(err, errlen, "gemmkit: internal error: MN-major operand not TMA-aligned");
+        return 1;
+    }
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(op.rows), static_cast<cuuint64_t>(K), 1};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(op.mn_ld),
+                             static_cast<cuuint64_t>(op.mn_ld) * static_cast<cuuint64_t>(K)};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapSwizzle sw = box_cols == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
+                                  : box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                   : CU_TENSOR_MAP_SWIZZLE_128B;
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(op.ptr), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        snprintf(err, errlen, "gemmkit: cuTensorMapEncodeTiled (MN-major) failed (%d)",
+                 static_cast<int>(r));
+        return 3;
+    }
+    TmapEntry& e = g_tmap_cache[g_tmap_next];
+    e.key = key;
+    e.map = *map;
+    e.dev = dev;
+    g_tmap_next = (g_tmap_next + 1) % TMAP_CACHE;
+    if (g_tmap_used < TMAP_CACHE) ++g_tmap_used;
+    return 0;
+}
+
 int encode_tiled_operand(CUtensorMap* map, const Operand& op, int64_t K, int box_rows, char* err,
                          size_t errlen) {
     PFN_tmapEncodeTiled enc = get_encode();
@@ -670,8 +721,18 @@ static int launch_one(const TcProblem& pr, const TcPlan& plan, GemmParams gp, ch
     int rc = 0;
     if (pr.a.slab == 0 && (rc = encode_operand(&ta, pr.a, pr.K, pr.batch, ES, BM, err, errlen)))
         return rc;
-    if (pr.b.slab == 0 && (rc = encode_operand(&tb, pr.b, pr.K, pr.batch, ES, BN, err, errlen)))
+    if (pr.b.mn_ld > 0) {
+        if (ES != 1 || (BN != 32 && BN != 64 && BN != 128)) {
+            snprintf(err, errlen, "gemmkit: internal error: MN-major operand for this kernel");
+            return 1;
+        }
+        rc = encode_mn_operand(&tb, pr.b, pr.K, BN, err, errlen);
+        if (rc) return rc;
+        gp.b_mn = 1;
+    } else if (pr.b.slab == 0 &&
+               (rc = encode_operand(&tb, pr.b, pr.K, pr.batch, ES, BN, err, errlen))) {
         return rc;
+    }
     if (pr.b.slab && (pr.b.rows % BN)) {
         snprintf(err, errlen, "gemmkit: internal error: tiled operand rows not padded to %d", BN);
         return 1;
@@ -750,6 +811,7 @@ void plan_tc_gemm(const TcProblem& p, bool allow_sk, TcPlan* plan) {
     TcPlan& pl = *plan;
     memset(&pl, 0, sizeof(pl));
     pl.bn = pick_bn(p);
+    if (p.b.mn_ld > 0 && pl.bn > 128) pl.bn = 128;  // an MN-major B box spans <= 128 bytes
     pl.nepi = pl.bn >= 64 ? 8 : 4;
     pl.tiles_m = static_cast<int>((p.Mk + BM - 1) / BM);
     pl.tiles_n = static_cast<int>((p.Nk + pl.bn - 1) / pl.bn);
@@ -782,7 +844,7 @@ void plan_tc_gemm(const TcProblem& p, bool allow_sk, TcPlan* plan) {
 
 void plan_tc_gemm2(const TcProblem& p, bool allow_sk, bool allow_pair, bool allow_gemv,
                    TcPlan* plan, bool allow_gemv_sk) {
-    if (allow_gemv && plan_gemv(p, plan, allow_gemv_sk)) return;
+    if (allow_gemv && p.b.mn_ld == 0 && plan_gemv(p, plan, allow_gemv_sk)) return;
     plan_tc_gemm(p, allow_sk, plan);
     TcPlan& pl = *plan;
     if (!allow_pair || pl.bn != 256 || p.Mk < 2 * BM) return;

@@ -178,6 +178,17 @@ class TileFamily:
                 gk.gemm_i8_packed_b_requant(m, a.data_ptr(), k, 1, packed, req, c.data_ptr(),
                                             1, m)
             self.calls.append((call, 2.0 * m * n * k / 1e12, keep))
+        # row-major A and B -> i32 (B read MN-major, or packed K-major)
+        r = 1024
+        ra = torch.randint(-128, 128, (r * r,), dtype=torch.int8, device="cuda", generator=g)
+        rb = torch.randint(-128, 128, (r * r,), dtype=torch.int8, device="cuda", generator=g)
+        rc = torch.empty(r * r, dtype=torch.int32, device="cuda")
+
+        def rcall(r=r, keep=(ra, rb, rc)):
+            ra, rb, rc = keep
+            gk.gemm_i8_unchecked(r, r, r, 1, ra.data_ptr(), r, 1, rb.data_ptr(), r, 1, 0,
+                                 rc.data_ptr(), r, 1)
+        self.calls.append((rcall, 2.0 * r ** 3 / 1e12, (ra, rb, rc)))
         s = 2048 if quick else 4096
         ha = torch.randn(s * s, device="cuda", generator=g).to(torch.bfloat16)
         hb = torch.randn(s * s, device="cuda", generator=g).to(torch.bfloat16)
@@ -303,6 +314,7 @@ KNOBS = {
     "GEMMKIT_CUDA_GEMV_SK": ([0, 1], ("small_m",)),
     "GEMMKIT_CUDA_GEMV_SPLIT": ([2, 4, 8], ("small_m",)),
     "GEMMKIT_CUDA_PDL": ([0, 1], ("small_m", "tile")),
+    "GEMMKIT_CUDA_MN_B": ([0, 1], ("tile",)),
 }
 
 

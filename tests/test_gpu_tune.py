@@ -87,6 +87,15 @@ def _parity_checks():
                                     req2, dc2.data_ptr(), n2, 1)
     assert np.array_equal(host(dc2).reshape(m2, n2),
                           _vnni(a2, b2, scales=sc2, scale_axis="row", zp=-3))
+    # row-major A and B -> i32 (B N-contiguous: read MN-major or packed)
+    m3, k3, n3 = 1000, 1000, 1000
+    a3 = rand_i8(rng, (m3, k3))
+    b3 = rand_i8(rng, (k3, n3))
+    da3, db3 = dev(a3), dev(b3)
+    dc3 = empty(m3 * n3, np.int32)
+    gk.gemm_i8_unchecked(m3, k3, n3, 1, da3.data_ptr(), k3, 1, db3.data_ptr(), n3, 1, 0,
+                         dc3.data_ptr(), n3, 1)
+    assert np.array_equal(host(dc3).reshape(m3, n3), O.gemm_i8_matrix(1, a3, b3, 0, None))
 
 
 def test_parity_under_tuned_profile():
@@ -94,7 +103,7 @@ def test_parity_under_tuned_profile():
     lines, and check a product of every shape class against the oracle; then restore."""
     before = {n: gk.knob_get(n) for n in gk.knob_names()}
     knobs = ("GEMMKIT_CUDA_BN,GEMMKIT_CUDA_BN_SHORTK,GEMMKIT_CUDA_EPI16,GEMMKIT_CUDA_STAGES,"
-             "GEMMKIT_CUDA_GEMV_SK,GEMMKIT_CUDA_GEMV_SPLIT")
+             "GEMMKIT_CUDA_GEMV_SK,GEMMKIT_CUDA_GEMV_SPLIT,GEMMKIT_CUDA_MN_B")
     results, profile = tune.run(["--quick", "--dry-run", "--reps", "3", "--batch-ms", "2",
                                  "--knobs", knobs])
     exports = [ln.split()[1].split("=") for ln in profile.splitlines()
