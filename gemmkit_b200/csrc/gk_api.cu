@@ -96,16 +96,18 @@ int check_device(int* dev_out) {
 //   GEMMKIT_CUDA_GEMV_SPLIT largest cluster K split of the small-M kernel (0 = up to 8)
 //   GEMMKIT_CUDA_MN_B     1 = an N-contiguous i8 B is read MN-major by the tile kernel (no
 //                         transpose pack; tiles at most 128 wide); 0 = packed K-major first
+//   GEMMKIT_CUDA_REQUANT_F32 1 = the 16-warp form requantizes an item in packed f32 when its
+//                         |acc + bias| < 2^22 and its scales are below 1 (exact there)
 enum KnobId {
     K_BN = 0, K_PAIR, K_GEMV, K_PDL, K_STREAMK, K_GEMVSK, K_BNSHORTK, K_EPI16, K_STAGES,
-    K_GEMVSPLIT, K_MNB, K_COUNT
+    K_GEMVSPLIT, K_MNB, K_F32Q, K_COUNT
 };
 const char* const kKnobEnv[K_COUNT] = {
     "GEMMKIT_CUDA_BN",       "GEMMKIT_CUDA_PAIR",      "GEMMKIT_CUDA_GEMV",
     "GEMMKIT_CUDA_PDL",      "GEMMKIT_CUDA_STREAMK",   "GEMMKIT_CUDA_GEMV_SK",
     "GEMMKIT_CUDA_BN_SHORTK", "GEMMKIT_CUDA_EPI16",    "GEMMKIT_CUDA_STAGES",
-    "GEMMKIT_CUDA_GEMV_SPLIT", "GEMMKIT_CUDA_MN_B"};
-const int64_t kKnobDefault[K_COUNT] = {0, 1, 1, 1, 0, 0, 0, 1, 0, 0, 1};
+    "GEMMKIT_CUDA_GEMV_SPLIT", "GEMMKIT_CUDA_MN_B", "GEMMKIT_CUDA_REQUANT_F32"};
+const int64_t kKnobDefault[K_COUNT] = {0, 1, 1, 1, 0, 0, 0, 1, 0, 0, 1, 1};
 std::atomic<int64_t> g_knob_set[K_COUNT];  // value + 1; 0 = no run-time override
 
 bool knob_valid(int id, int64_t v) {
@@ -439,7 +441,10 @@ int execute(const Job& j) {
     e.scales = j.scales;
     e.scale_bs = j.scale_bs;
     e.scale = j.scale;
-    e.zp = j.zp;
+    // The kernels add zp to the rounded product (|rne| < 2^22 on every path) in 32-bit
+    // integers; the reference adds it in 64 bits with saturation. Clamping zp to +-2^30 keeps
+    // the 32-bit sum exact, and any zp past that drives the output to the same band edge.
+    e.zp = j.zp < -(1 << 30) ? -(1 << 30) : (j.zp > (1 << 30) ? (1 << 30) : j.zp);
     e.lo = j.lo;
     e.hi = j.hi;
     e.relu = j.out == gk::Out::Q8 && j.lo > (j.hi == 255 ? 0 : -128);
@@ -556,6 +561,7 @@ int execute(const Job& j) {
     pr.stages = static_cast<int>(knob(K_STAGES));
     pr.epi16 = static_cast<int>(knob(K_EPI16));
     pr.gemv_split = static_cast<int>(knob(K_GEMVSPLIT));
+    pr.f32q = static_cast<int>(knob(K_F32Q));
     // An N-contiguous i8 right-hand side (row-major B of C = A*B) is read MN-major by the
     // tile kernel's TMA, with no transpose pack: rows contiguous, K at a 16-byte pitch.
     if (need[1] && j.kind == gk::Kind::I8 && j.batch == 1 && kb.rs == 1 && kb.ks >= kb.rows &&
@@ -697,7 +703,8 @@ void gk_workspace_free(gk_workspace* ws) {
 const char* gk_knob_names(void) {
     return "GEMMKIT_CUDA_BN,GEMMKIT_CUDA_PAIR,GEMMKIT_CUDA_GEMV,GEMMKIT_CUDA_PDL,"
            "GEMMKIT_CUDA_STREAMK,GEMMKIT_CUDA_GEMV_SK,GEMMKIT_CUDA_BN_SHORTK,GEMMKIT_CUDA_EPI16,"
-           "GEMMKIT_CUDA_STAGES,GEMMKIT_CUDA_GEMV_SPLIT,GEMMKIT_CUDA_MN_B";
+           "GEMMKIT_CUDA_STAGES,GEMMKIT_CUDA_GEMV_SPLIT,GEMMKIT_CUDA_MN_B,"
+           "GEMMKIT_CUDA_REQUANT_F32";
 }
 
 int gk_knob_get(const char* name, int64_t* value) {

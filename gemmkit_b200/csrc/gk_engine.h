@@ -84,7 +84,8 @@ struct GemmParams {
     uint32_t sk_epoch;
     uint64_t timeout_ns;
     unsigned int* status;
-    int32_t stages;  // ring depth cap (0: the kernel's whole ring)
+    int32_t stages;
+    int32_t f32q;  // 1: the pair kernel's 16-warp form may requantize items in packed f32  // ring depth cap (0: the kernel's whole ring)
     EpiParams e;
 };
 
@@ -116,6 +117,7 @@ struct TcProblem {
     int stages;  // ring depth cap of the kernels (0: their whole ring)
     int epi16;   // 1: the CTA-pair kernel may take its 16-warp epilogue form (short K)
     int gemv_split;  // small-M kernel: largest cluster K split (0: up to 8)
+    int f32q;        // 1: short-K requantized items may take the packed f32 path
     // Scratch for a stream-K tail (see GemmParams); nullptr = no stream-K.
     uint32_t* sk_part;
     uint32_t* sk_ctr;

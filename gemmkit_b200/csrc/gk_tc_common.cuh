@@ -91,6 +91,33 @@ __device__ __forceinline__ int requant_q_small(uint32_t acc, uint32_t bias_plus,
     return q;
 }
 
+// The same requantize for two elements in packed f32x2 arithmetic, for items whose values
+// v = acc + bias all satisfy |v| < 2^22 and whose scale s (f32) is below 1. Then fl64(v * s) is
+// v * s exactly (22 + 24 significant bits), |v * s| < 2^22, and one f32 FMA gives it rounded
+// half-even: fma(v, s, 1.5 * 2^23) lies in [2^23, 2^24), where the f32 spacing is 1, so the
+// single rounding of the exact sum is 1.5 * 2^23 + rne(v * s) (1.5 * 2^23 is even: ties keep
+// their parity). v enters as f32 through its bit pattern: bias_f carries bias + 0x4B400000, so
+// acc + bias_f is the pattern of 1.5 * 2^23 + v and subtracting 1.5 * 2^23 leaves v exactly.
+// The result's pattern minus qoff = 0x4B400000 - zp is rne(v * s) + zp for any zero point
+// with |zp| <= 2^30. ss holds s in both halves. Per pair: two adds, one add.f32x2, one
+// fma.f32x2, two subtracts.
+__device__ __forceinline__ void requant_pair_f32(uint32_t acc0, uint32_t acc1, uint32_t bias0,
+                                                 uint32_t bias1, uint64_t ss, uint32_t qoff,
+                                                 int& q0, int& q1) {
+    asm("{\n\t.reg .b32 a, b;\n\t.reg .b64 e, y;\n\t"
+        "add.u32 a, %2, %4;\n\t"
+        "add.u32 b, %3, %5;\n\t"
+        "mov.b64 e, {a, b};\n\t"
+        "add.rn.f32x2 e, e, %6;\n\t"
+        "fma.rn.f32x2 y, e, %7, %8;\n\t"
+        "mov.b64 {a, b}, y;\n\t"
+        "sub.u32 %0, a, %9;\n\t"
+        "sub.u32 %1, b, %9;\n\t}"
+        : "=r"(q0), "=r"(q1)
+        : "r"(acc0), "r"(acc1), "r"(bias0), "r"(bias1), "l"(0xCB400000CB400000ull), "l"(ss),
+          "l"(0x4B4000004B400000ull), "r"(qoff));
+}
+
 // Four values saturated to the output band and packed little-endian (x0 in the low byte).
 template <bool U8>
 __device__ __forceinline__ uint32_t pack4_sat(int x0, int x1, int x2, int x3) {
@@ -228,7 +255,9 @@ __device__ __forceinline__ void out_1(const EpiParams& e, int64_t elem_off, T v)
 // loop is straight-line code: the general path takes every axis, zero point and scale; the two
 // short ones take a per-row (or per-tensor) scale of at most 2^-9 with an even zero point
 // (requant_q_small), with the bias per column (compact array) or per row / none (register).
-enum QuantMode { QM_GENERAL = 0, QM_SMALL_COLB = 1, QM_SMALL_ROWB = 2 };
+// QM_F32 (the CTA-pair kernel's 16-warp form only) takes items whose |acc + bias| < 2^22 and
+// whose scales are below 1 through requant_pair_f32.
+enum QuantMode { QM_GENERAL = 0, QM_SMALL_COLB = 1, QM_SMALL_ROWB = 2, QM_F32 = 3 };
 
 // The quant mode of this warp's rows for the current tile; every lane of the warp calls it.
 __device__ __forceinline__ int pick_quant_mode(const EpiParams& e, double r_se) {

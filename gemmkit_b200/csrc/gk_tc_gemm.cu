@@ -896,6 +896,7 @@ int launch_tc_gemm_planned(const TcProblem& pr, const TcPlan& plan, char* err, s
     gp.timeout_ns = 4000000000ull;
     gp.status = device_status_ptr();
     gp.stages = pr.stages;
+    gp.f32q = pr.f32q;
     gp.e = pr.e;
     if (plan.gemv) return launch_gemv(pr, plan, err, errlen);
     if (plan.pair) return launch_pair(pr, plan, gp, err, errlen);

@@ -122,7 +122,10 @@ __device__ __forceinline__ void pair_item(int t, const GemmParams& p, int& tile,
 // piece j ^ ((r >> 1) & 3), conflict-free) and one TMA tensor store of the block at (x, y, z)
 // of tmC writes it to C; the store clips rows and columns past C. The caller has made sure the
 // store that last read sblk is done.
-template <bool SMALL, bool BCOL, bool RELU, bool U8, int CH, int NCH, bool TMA = false>
+// MODE: 0 the general requantize (requant_q with clamps), 1 the short one (requant_q_small),
+// 2 the packed f32 one (requant_pair_f32: se then holds the f32 scale in both halves of its
+// bits and the biases are bias + 0x4B400000).
+template <int MODE, bool BCOL, bool RELU, bool U8, int CH, int NCH, bool TMA = false>
 __device__ __forceinline__ void quant_rows_fast(uint32_t tbase, int nch, int64_t ncol,
                                                 uint8_t* dst, bool row_ok, uint32_t bslice,
                                                 double se, double nms, double magic,
@@ -133,7 +136,8 @@ __device__ __forceinline__ void quant_rows_fast(uint32_t tbase, int nch, int64_t
                                                 int y = 0, int z = 0) {
     // 32-column chunks (8 epilogue warps) keep the next chunk's TMEM load in flight; 16-column
     // chunks (16 warps, 96 registers) load one chunk at a time and rely on the other warps.
-    constexpr bool DB = CH == 32;
+    constexpr bool DB = CH == 32 || TMA;
+    if constexpr (TMA) nch = NCH;  // a TMA-stored block is always the warp's whole width
     uint32_t va[32], vb[32];
     tmem_ld_chunk<CH>(tbase, va);
 #pragma unroll
@@ -157,11 +161,18 @@ __device__ __forceinline__ void quant_rows_fast(uint32_t tbase, int nch, int64_t
             if constexpr (BCOL) bq = ld_shared_v4(bslice + static_cast<uint32_t>(c * CH + 4 * g) * 4u);
             const uint32_t bs[4] = {bq.x, bq.y, bq.z, bq.w};
             int qv[4];
+            if constexpr (MODE == 2) {
+                const uint64_t ss = static_cast<uint64_t>(__double_as_longlong(se));
+                const uint32_t qoff = 0x4B400000u - static_cast<uint32_t>(zp);
+                requant_pair_f32(cur[4 * g], cur[4 * g + 1], bs[0], bs[1], ss, qoff, qv[0], qv[1]);
+                requant_pair_f32(cur[4 * g + 2], cur[4 * g + 3], bs[2], bs[3], ss, qoff, qv[2],
+                                 qv[3]);
+            }
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
-                if constexpr (SMALL)
+                if constexpr (MODE == 1)
                     qv[t] = requant_q_small(cur[4 * g + t], bs[t], se, nms, magic);
-                else
+                else if constexpr (MODE == 0)
                     qv[t] = requant_q(cur[4 * g + t], bs[t], se, nms, ulo, uhi, zp);
                 if constexpr (RELU) qv[t] = max(qv[t], lo);
             }
@@ -449,9 +460,36 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
             uint2* rowclamp = reinterpret_cast<uint2*>(pb + C::PB_CLAMP);
             uint32_t* colb = reinterpret_cast<uint32_t*>(pb + C::PB_COLB);
             ItemPar* ip = reinterpret_cast<ItemPar*>(pb + C::PB_POS);
+            // The packed f32 path takes the whole item when every |acc + bias| < 2^22
+            // (|acc| <= K * 2^14 for i8 operands) and every scale is below 1.
+            bool f32 = false;
+            if (p.f32q) {
+                uint32_t mb = 0;
+                bool s_ok = true;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    mb = max(mb, static_cast<uint32_t>(abs(L.rb[j])));
+                    s_ok = s_ok && L.sc[j] < 1.0f;
+                }
+#pragma unroll
+                for (int i = 0; i < BN / 32; ++i) mb = max(mb, static_cast<uint32_t>(abs(L.cb[i])));
+                mb = __reduce_max_sync(0xffffffffu, mb);
+                f32 = __all_sync(0xffffffffu, s_ok) &&
+                      static_cast<int64_t>(p.K) * 16384 + mb < (int64_t{1} << 22) &&
+                      e.zp >= -(1 << 30) && e.zp <= (1 << 30);
+            }
+            const uint32_t boff = f32 ? 0x4B400000u : 0x80000000u;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int r = lane + 32 * j;
+                if (f32) {
+                    const uint64_t ss = (static_cast<uint64_t>(__float_as_uint(L.sc[j])) << 32) |
+                                        __float_as_uint(L.sc[j]);
+                    rowse[r] = make_double2(__longlong_as_double(static_cast<long long>(ss)), 0.0);
+                    rowbp[r] = static_cast<uint32_t>(L.rb[j]) + boff;
+                    if (lane == 0) ip->qmode[j] = QM_F32;
+                    continue;
+                }
                 double se, nms;
                 make_scale_se(L.sc[j], se, nms);
                 rowse[r] = make_double2(se, nms);
@@ -469,7 +507,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
             }
 #pragma unroll
             for (int i = 0; i < BN / 32; ++i)
-                colb[lane + 32 * i] = static_cast<uint32_t>(L.cb[i]) + 0x80000000u;
+                colb[lane + 32 * i] = static_cast<uint32_t>(L.cb[i]) + boff;
             if (lane == 0) {
                 ip->b = L.b;
                 ip->tm = L.tm;
@@ -534,8 +572,8 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
             tc_fence_after();
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * BN + col_base);
-            auto run = [&](auto small_tag, auto bcol_tag, auto relu_tag) {
-                constexpr bool SM = decltype(small_tag)::value;
+            auto run = [&](auto mode_tag, auto bcol_tag, auto relu_tag) {
+                constexpr int SM = decltype(mode_tag)::value;
                 constexpr bool BC = decltype(bcol_tag)::value;
                 constexpr bool RL = decltype(relu_tag)::value;
                 if (tma)
@@ -550,19 +588,19 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
             };
             using T = std::true_type;
             using F = std::false_type;
-            if (qm != QM_GENERAL) {
+            auto by_axes = [&](auto mode_tag) {
                 if (bcol) {
-                    if (relu) run(T{}, T{}, T{}); else run(T{}, T{}, F{});
+                    if (relu) run(mode_tag, T{}, T{}); else run(mode_tag, T{}, F{});
                 } else {
-                    if (relu) run(T{}, F{}, T{}); else run(T{}, F{}, F{});
+                    if (relu) run(mode_tag, F{}, T{}); else run(mode_tag, F{}, F{});
                 }
-            } else {
-                if (bcol) {
-                    if (relu) run(F{}, T{}, T{}); else run(F{}, T{}, F{});
-                } else {
-                    if (relu) run(F{}, F{}, T{}); else run(F{}, F{}, F{});
-                }
-            }
+            };
+            if (qm == QM_F32)
+                by_axes(std::integral_constant<int, 2>{});
+            else if (qm != QM_GENERAL)
+                by_axes(std::integral_constant<int, 1>{});
+            else
+                by_axes(std::integral_constant<int, 0>{});
             __syncwarp();
             if (lane == 0) mbar_arrive(&pfree[buf]);  // this item's parameters are read
         }
@@ -733,7 +771,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
                         constexpr bool RL = decltype(relu_tag)::value;
                         if constexpr (EPI16) {
                             if (tma) {
-                                quant_rows_fast<SM, BC, RL, U8, CH, NCH, true>(
+                                quant_rows_fast<SM ? 1 : 0, BC, RL, U8, CH, NCH, true>(
                                     tbase, nch, p.Nk - (gcol0 + col_base), dst, row_ok, bslice,
                                     r_se, r_nms, magic, r_bp, r_ulo, r_uhi, e.zp, e.lo,
                                     tempty_l + 8u * acc, lane, sblk, &tmC,
@@ -741,7 +779,7 @@ __global__ void __launch_bounds__(PairCfg<OUT, BN, EPI16>::THREADS, 1)
                                 return;
                             }
                         }
-                        quant_rows_fast<SM, BC, RL, U8, CH, NCH>(
+                        quant_rows_fast<SM ? 1 : 0, BC, RL, U8, CH, NCH>(
                             tbase, nch, p.Nk - (gcol0 + col_base), dst, row_ok, bslice, r_se,
                             r_nms, magic, r_bp, r_ulo, r_uhi, e.zp, e.lo, tempty_l + 8u * acc,
                             lane);

@@ -238,7 +238,7 @@ def test_knobs_get_set_and_validation():
     assert names == ["GEMMKIT_CUDA_BN", "GEMMKIT_CUDA_PAIR", "GEMMKIT_CUDA_GEMV",
                      "GEMMKIT_CUDA_PDL", "GEMMKIT_CUDA_STREAMK", "GEMMKIT_CUDA_GEMV_SK",
                      "GEMMKIT_CUDA_BN_SHORTK", "GEMMKIT_CUDA_EPI16", "GEMMKIT_CUDA_STAGES",
-                     "GEMMKIT_CUDA_GEMV_SPLIT", "GEMMKIT_CUDA_MN_B"]
+                     "GEMMKIT_CUDA_GEMV_SPLIT", "GEMMKIT_CUDA_MN_B", "GEMMKIT_CUDA_REQUANT_F32"]
     base = {n: gk.knob_get(n) for n in names}
     try:
         gk.knob_set("GEMMKIT_CUDA_BN", 128)

@@ -117,10 +117,13 @@ def test_knob_paths_batched_requant(kv):
 EPI16_SHAPES = [(2341, 200, 2315), (2313, 77, 2339)]
 
 
+@pytest.mark.parametrize("f32", [1, 0])
 @pytest.mark.parametrize("out_u8", [False, True])
 @pytest.mark.parametrize("axes", [("col", "col"), ("row", "col"), ("col", "row"), ("row", "row")])
 @pytest.mark.parametrize("shape", EPI16_SHAPES, ids=lambda s: "x".join(map(str, s)))
-def test_pair_epi16_requant(shape, axes, out_u8):
+def test_pair_epi16_requant(shape, axes, out_u8, f32):
+    """With GEMMKIT_CUDA_REQUANT_F32=1 these items take the packed f32 requantize (|acc + bias|
+    < 2^22, scales below 1); with 0 the f64 short and general paths."""
     m, k, n = shape
     scale_axis, bias_axis = axes
     rng = np.random.default_rng(m + k + 3 * out_u8 + 7 * len(scale_axis + bias_axis))
@@ -141,10 +144,69 @@ def test_pair_epi16_requant(shape, axes, out_u8):
     for c_row in (True, False):
         dc = empty(m * n, np.uint8 if out_u8 else np.int8)
         rsc, csc = (n, 1) if c_row else (1, m)
-        gk.gemm_i8_requant_ex_unchecked(m, k, n, ptr(da), k, 1, ptr(dbT), 1, k, req, ptr(dc),
-                                        rsc, csc, out_u8=out_u8)
+        with knobs(GEMMKIT_CUDA_REQUANT_F32=f32):
+            gk.gemm_i8_requant_ex_unchecked(m, k, n, ptr(da), k, 1, ptr(dbT), 1, k, req, ptr(dc),
+                                            rsc, csc, out_u8=out_u8)
         got = gather(host(dc), m, n, rsc, csc)
         assert np.array_equal(got, want), (c_row, axes)
+
+
+def _epi16_call(a, bT, req, out_u8):
+    """Row-major C, so a per-row scale stays on the kernel's rows (the 16-warp form's case)."""
+    m, k = a.shape
+    n = bT.shape[0]
+    da, dbT = dev(a), dev(bT)
+    dc = empty(m * n, np.uint8 if out_u8 else np.int8)
+    gk.gemm_i8_requant_ex_unchecked(m, k, n, ptr(da), k, 1, ptr(dbT), 1, k, req, ptr(dc), n, 1,
+                                    out_u8=out_u8)
+    return host(dc).reshape(m, n)
+
+
+@pytest.mark.parametrize("edge", ["at_bound", "past_bound"])
+def test_pair_epi16_f32_range_bound(edge):
+    """The packed f32 requantize needs |acc + bias| < 2^22: A = B = -128 everywhere makes every
+    accumulator K * 2^14, and biases of magnitude 2^22 - K * 2^14 - 1 (the f32 path) or
+    2^22 - K * 2^14 (the item falls back to the f64 path). Scales near 3e-5 put the results
+    across the band; odd zero points; rows with a scale of 1.5 (fallback) in a third call."""
+    m, k, n = 2304, 128, 2304
+    a = np.full((m, k), -128, np.int8)
+    bT = np.full((n, k), -128, np.int8)
+    top = (1 << 22) - k * 16384 - (1 if edge == "at_bound" else 0)
+    rng = np.random.default_rng(4 + len(edge))
+    bias = np.where(rng.random(n) < 0.5, top, -top).astype(np.int32)
+    bias[::7] = rng.integers(-1000, 1000, len(bias[::7]))
+    dbias = dev(bias)
+    for scales, zp, out_u8 in ((rng.uniform(2.5e-5, 3e-5, m), -7, False),
+                               (rng.uniform(2.5e-5, 3e-5, m), 129, True),
+                               (np.where(rng.random(m) < 0.1, 1.5, 2.9e-5), 3, False)):
+        scales = scales.astype(np.float32)
+        dsc = dev(scales)
+        want = vnni_requant(a, bT, scales=scales, scale_axis="row", bias=bias, bias_axis="col",
+                            zp=zp, out_u8=out_u8)
+        req = gk.Requantize(gk.RequantScale.PerRow(dsc), zp, dbias, gk.AXIS_COL)
+        for f32 in (1, 0):
+            with knobs(GEMMKIT_CUDA_REQUANT_F32=f32):
+                got = _epi16_call(a, bT, req, out_u8)
+            assert np.array_equal(got, want), (edge, zp, f32)
+
+
+@pytest.mark.parametrize("shape", [(2304, 200, 2304), (1100, 700, 1300), (300, 300, 300),
+                                   (8, 4096, 2048)], ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("zp", [-(1 << 30), (1 << 30), (1 << 30) + 1, -2**31, 2**31 - 1])
+def test_zero_point_limits(zp, shape):
+    """Zero points at and past +-2^30 (the engine clamps zp there; the reference adds it in 64
+    bits with saturation), per-tensor scale on both sides of 2^-9, a per-row bias, ReLU, on the
+    16-warp form, the 8-warp pair kernel, the tile kernel and the small-M kernel."""
+    rng = np.random.default_rng(zp & 0xFFFF)
+    m, k, n = shape
+    a = rand_i8(rng, (m, k))
+    bT = rand_i8(rng, (n, k))
+    bias = rng.integers(-2**15, 2**15 + 1, m).astype(np.int32)
+    dbias = dev(bias)
+    for scale in (3e-4, 0.9, 5e-3):
+        want = vnni_requant(a, bT, scale=scale, bias=bias, bias_axis="row", zp=zp, relu=True)
+        req = gk.Requantize(gk.RequantScale.PerTensor(scale), zp, dbias, gk.AXIS_ROW, True)
+        assert np.array_equal(_epi16_call(a, bT, req, False), want), scale
 
 
 @pytest.mark.parametrize("sk", [0, 1])
