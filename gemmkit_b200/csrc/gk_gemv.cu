@@ -64,6 +64,7 @@ struct GemvParams {
     uint32_t* ctr;
     uint32_t epoch;
     int32_t early_weights;   // fetch the first ring of weights before griddep_wait
+
     const uint8_t* w_tiled;  // tiled prepacked weights, or nullptr: load through the tensor map
     int64_t w_slab;          // bytes between consecutive K blocks of w_tiled
     uint64_t timeout_ns;
@@ -97,7 +98,7 @@ struct GemvCfg {
     static constexpr int SMEM = 1024 + RING_BYTES + BAR_BYTES + CP_BYTES;
     static constexpr int CH = NB == 16 ? 16 : 32;  // TMEM columns per load
     static constexpr int NCH = NB / CH;
-    static_assert(SMEM <= SMEM_LIMIT, "gemv stages exceed shared memory");
+    static_assert(SMEM + static_cast<int>(sizeof(EpiParams)) <= SMEM_LIMIT, "gemv stages exceed shared memory");
     static_assert((STAGE_BYTES % 1024) == 0, "stages must keep the 1024-byte swizzle alignment");
     static_assert((2 * STAGES + 2 * NACC + 1) * 8 + 8 <= BAR_BYTES, "barrier area");
 };
@@ -317,6 +318,12 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
         tmem_alloc(tmem_slot, C::TMEM_COLS);
         tmem_relinquish();
     }
+    // The epilogue's parameters, copied to shared memory while the CTA starts: read from the
+    // kernel's parameter space for the first time after the last accumulator is ready, each
+    // field's constant-cache miss lands on the call's tail (about a microsecond in all).
+    __shared__ EpiParams s_epi;
+    for (int i = threadIdx.x; i < static_cast<int>(sizeof(EpiParams) / 4); i += blockDim.x)
+        reinterpret_cast<uint32_t*>(&s_epi)[i] = reinterpret_cast<const uint32_t*>(&p.e)[i];
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -544,7 +551,7 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         const int et = threadIdx.x - 64;
-        const EpiParams& e = p.e;
+        const EpiParams& e = s_epi;
         griddep_wait();  // scales, bias and the output may belong to the previous kernel
         if (QUANT && (e.scale_axis == AX_N || e.bias_axis == AX_N)) {
             if (et < NB) {
@@ -573,20 +580,25 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
             if (p.sk && n >= C::NACC) break;
             grow = static_cast<int64_t>(tile) * BM + row;
             const bool row_ok = grow < p.Mk;
-            // this row's requant constants, fetched while the MMAs run
+            // this row's requant constants, fetched while the MMAs run (loads issued before the
+            // accumulator wait: with one item per CTA their latency is otherwise the call's tail)
             if constexpr (OUT == Out::F32)
-                r_fb = (e.fbias_axis == AX_M && row_ok) ? e.fbias[grow] : 0.0f;
+                r_fb = (e.fbias_axis == AX_M && row_ok)
+                           ? __uint_as_float(ld_global_issue_u32(e.fbias + grow)) : 0.0f;
             if constexpr (OUT == Out::I32)  // the fused i32 epilogue's per-row bias
-                r_bp = (e.bias_axis == AX_M && row_ok) ? static_cast<uint32_t>(e.bias[grow]) : 0u;
+                r_bp = (e.bias_axis == AX_M && row_ok) ? ld_global_issue_u32(e.bias + grow) : 0u;
             if constexpr (QUANT) {
                 float rs = e.scale;
-                int32_t rb = 0;
+                uint32_t rb = 0;
                 if (row_ok) {
-                    if (e.scale_axis == AX_M) rs = e.scales[grow];
-                    if (e.bias_axis == AX_M) rb = e.bias[grow];
+                    if (e.scale_axis == AX_M)
+                        rs = __uint_as_float(ld_global_issue_u32(e.scales + grow));
+                    if (e.bias_axis == AX_M) rb = ld_global_issue_u32(e.bias + grow);
                 }
                 if (e.scale_axis != AX_N) make_scale_param(rs, r_se, r_nms, r_ulo, r_uhi);
-                r_bp = static_cast<uint32_t>(rb) + 0x80000000u;
+                r_bp = rb + 0x80000000u;
+                // the constants are computed here, not after the accumulator wait
+                asm volatile("" ::"d"(r_se), "d"(r_nms), "r"(r_ulo), "r"(r_uhi), "r"(r_bp));
             }
             // A finisher gathers the writers' partials of its 32 rows while its own last MMAs
             // run: it waits (bounded) until the tile's writers have counted in, then sums their
@@ -817,6 +829,7 @@ static int launch_gemv_nb(const TcProblem& pr, const TcPlan& plan, GemvParams gp
     }
     gp.w_tiled = pr.a.slab ? static_cast<const uint8_t*>(pr.a.ptr) : nullptr;
     gp.w_slab = pr.a.slab;
+
     auto kern = gemv_kernel<KIND, OUT, NB>;
     static int attr_done[64] = {0};
     int dev = 0;

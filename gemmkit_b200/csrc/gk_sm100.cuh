@@ -63,19 +63,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase of `parity` to complete. Gives up when the CTA-wide abort flag
 // is raised by another role or after `timeout_ns`; the first role to time out raises the
-// flag and records `where` in the device status word. Returns false on give-up.
+// flag and records `where` in the device status word. Returns false on give-up. The flag and
+// the clock are looked at every 32nd poll only: a waiting warp then spends a few issue slots
+// per poll, which matters where many warps wait beside warps that compute. SLEEP_NS > 0 backs
+// off between polls instead (for waits of many warps at once that are not latency-critical).
+template <int SLEEP_NS = 0>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           unsigned int* status, unsigned int where,
                                           uint64_t timeout_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    while (true) {
+#pragma unroll 1
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
-        if (globaltimer_ns() - t0 > timeout_ns) {
-            *abort_flag = 1;
-            if (status) atomicOr(status, where);
-            return false;
+        if constexpr (SLEEP_NS > 0) __nanosleep(SLEEP_NS);
+        if (SLEEP_NS > 0 || (i & 31u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > timeout_ns) {
+                *abort_flag = 1;
+                if (status) atomicOr(status, where);
+                return false;
+            }
         }
     }
 }
@@ -125,6 +133,15 @@ __device__ __forceinline__ void bulk_wait_group_all() {
 // (a TMA store of the same bytes).
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 32-bit global loads issued exactly here: as volatile asm they stay ahead of the waits that
+// follow them, so their latency passes during the wait (a plain load of read-only data may be
+// scheduled after the wait, next to its first use).
+__device__ __forceinline__ uint32_t ld_global_issue_u32(const void* p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
@@ -444,6 +461,16 @@ __device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, ui
 
 // Arrive (once) on the mbarrier at shared::cluster address `caddr` -- in this CTA or the peer
 // -- when every pair MMA this thread issued so far has completed.
+// One commit that arrives on the barrier at shared-memory offset `saddr` in every CTA of
+// `cta_mask` (the pair: 0x3) once the MMAs issued so far are done (a commit, not a copy).
+__device__ __forceinline__ void mma_commit_pair_both(uint32_t saddr, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+        "[%0], %1;" ::"r"(saddr),
+        "h"(cta_mask)
+        : "memory");
+}
+
 __device__ __forceinline__ void mma_commit_pair(uint32_t caddr) {
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      caddr)

@@ -206,10 +206,11 @@ struct Sched {
     }
 };
 
+template <int SLEEP_NS = 0>
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           unsigned int* status, unsigned int where,
                                           uint64_t timeout) {
-    const bool ok = mbar_wait(bar, parity, abort_flag, status, where, timeout);
+    const bool ok = mbar_wait<SLEEP_NS>(bar, parity, abort_flag, status, where, timeout);
     return !__any_sync(0xffffffffu, !ok);
 }
 

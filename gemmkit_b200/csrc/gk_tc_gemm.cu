@@ -56,7 +56,7 @@ struct TileCfg {
     static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
                                      : (2 * BN <= 256) ? 256 : 512;  // a power of two
     static_assert(STAGES >= 2, "shared memory too small");
-    static_assert(SMEM <= SMEM_LIMIT, "shared memory budget");
+    static_assert(SMEM + static_cast<int>(sizeof(EpiParams)) <= SMEM_LIMIT, "shared memory budget");
     static_assert(2 * STAGES + 7 <= BAR_BYTES / 8 - 1, "barrier area");
 };
 
@@ -117,6 +117,12 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
         tmem_alloc(tmem_slot, C::TMEM_COLS);
         tmem_relinquish();
     }
+    // The epilogue's parameters in shared memory, copied while the CTA starts (first reads
+    // of the parameter space after the accumulator wait put constant-cache misses on the
+    // critical path of a CTA's only tile).
+    __shared__ EpiParams s_epi;
+    for (int i = threadIdx.x; i < static_cast<int>(sizeof(EpiParams) / 4); i += blockDim.x)
+        reinterpret_cast<uint32_t*>(&s_epi)[i] = reinterpret_cast<const uint32_t*>(&p.e)[i];
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -241,7 +247,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
         const int q = warp & 3;                             // TMEM lane quarter it may read
         const int col_base = ((warp - 2) >> 2) * C::WCOLS;  // its share of the tile's columns
         const int et = threadIdx.x - 64;                    // < NEPI_T, and BN <= NEPI_T
-        const EpiParams& e = p.e;
+        const EpiParams& e = s_epi;
         const int row = q * 32 + lane;
         const bool col_params = C::QUANT && (e.scale_axis == AX_N || e.bias_axis == AX_N);
 
