@@ -64,6 +64,10 @@ struct GemvParams {
     uint32_t* ctr;
     uint32_t epoch;
     int32_t early_weights;   // fetch the first ring of weights before griddep_wait
+    // the activation rows (Nk of them, x_row_bytes each at a pitch of x_ld bytes), for an L2
+    // prefetch hint before griddep_wait
+    const uint8_t* x;
+    int64_t x_ld, x_row_bytes;
 
     const uint8_t* w_tiled;  // tiled prepacked weights, or nullptr: load through the tensor map
     int64_t w_slab;          // bytes between consecutive K blocks of w_tiled
@@ -552,6 +556,18 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
         // ---------------- epilogue (warps 2..5) ----------------
         const int et = threadIdx.x - 64;
         const EpiParams& e = s_epi;
+        // Hint the activation rows into L2 (128-byte lines spread over the grid's epilogue
+        // threads): their first TMA loads after the dependency wait start the call's MMAs. A
+        // hint only; the loads read whatever the previous kernel wrote.
+        if (p.early_weights) {
+            const int64_t lines_per_row = (p.x_row_bytes + 127) / 128;
+            const int64_t lines = lines_per_row * p.Nk;
+            for (int64_t l = static_cast<int64_t>(blockIdx.x) * 128 + et; l < lines;
+                 l += static_cast<int64_t>(gridDim.x) * 128) {
+                const int64_t r = l / lines_per_row, c = (l - r * lines_per_row) * 128;
+                prefetch_l2(p.x + r * p.x_ld + c);
+            }
+        }
         griddep_wait();  // scales, bias and the output may belong to the previous kernel
         if (QUANT && (e.scale_axis == AX_N || e.bias_axis == AX_N)) {
             if (et < NB) {
@@ -829,6 +845,9 @@ static int launch_gemv_nb(const TcProblem& pr, const TcPlan& plan, GemvParams gp
     }
     gp.w_tiled = pr.a.slab ? static_cast<const uint8_t*>(pr.a.ptr) : nullptr;
     gp.w_slab = pr.a.slab;
+    gp.x = static_cast<const uint8_t*>(pr.b.ptr);
+    gp.x_ld = pr.b.ld * ES;
+    gp.x_row_bytes = pr.K * ES;
 
     auto kern = gemv_kernel<KIND, OUT, NB>;
     static int attr_done[64] = {0};

@@ -135,6 +135,11 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// L2 prefetch of the 128-byte line holding p (a hint; never faults on a valid address).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // 32-bit global loads issued exactly here: as volatile asm they stay ahead of the waits that
 // follow them, so their latency passes during the wait (a plain load of read-only data may be
 // scheduled after the wait, next to its first use).

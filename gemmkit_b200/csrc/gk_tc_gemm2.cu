@@ -139,8 +139,9 @@ __device__ __forceinline__ void quant_rows_fast(uint32_t tbase, int nch, int64_t
                                                 uint8_t* sblk = nullptr,
                                                 const CUtensorMap* tmC = nullptr, int x = 0,
                                                 int y = 0, int z = 0) {
-    // 32-column chunks (8 epilogue warps) keep the next chunk's TMEM load in flight; 16-column
-    // chunks (16 warps, 96 registers) load one chunk at a time and rely on the other warps.
+    // The next chunk's TMEM load is kept in flight while a chunk is requantized (32-column
+    // chunks of the 8-warp form, and the 16-warp form's TMA path); the 16-warp form's plain
+    // stores (cut items) load one chunk at a time.
     constexpr bool DB = CH == 32 || TMA;
     if constexpr (TMA) nch = NCH;  // a TMA-stored block is always the warp's whole width
     uint32_t va[32], vb[32];
