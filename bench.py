@@ -604,7 +604,13 @@ def measure_single(args, ws, peaks) -> dict:
     for key, cls, how in specs:
         w = cls(7)
         steps = max(args.steps, 20)
+        sampler = ClockSampler(torch.cuda.current_device(), 0.005) \
+            if not torch.distributed.is_initialized() or torch.distributed.get_rank() == 0 \
+            else None
+        if sampler:
+            sampler.start()
         ms = time_steps(w.step, steps, max(args.warmup, 3), ws) / steps
+        clocks = sampler.stop() if sampler else None
         eager_ms = ms
         if key == "c1":
             gms = graph_step_ms(w, 100, ws)
@@ -616,17 +622,26 @@ def measure_single(args, ws, peaks) -> dict:
         else:
             kval = w.work / (ms * 1e-3) / 1e12
             mult = 2.0 if w.unit == "TOPS" else 1.0
-            peak = peaks["bf16_tflops"] * mult
-            psrc = (f"2 x bf16_tflops of {peaks['source']} peaks (dense int8 = 2 x dense bf16)"
-                    if mult == 2.0 else f"bf16_tflops of {peaks['source']} peaks")
+            # A timed region of more than ~0.2 s of dense MMA runs under the 1 kW power cap:
+            # its peak is the sustained cuBLAS figure (seconds back to back), a shorter one
+            # is compared with the burst figure; both fractions are reported.
+            long_run = steps * eager_ms > 200.0 and peaks.get("bf16_tflops_sustained")
+            name = "bf16_tflops_sustained" if long_run else "bf16_tflops"
+            peak = peaks[name] * mult
+            psrc = (f"2 x {name} of {peaks['source']} peaks (dense int8 = 2 x dense bf16)"
+                    if mult == 2.0 else f"{name} of {peaks['source']} peaks")
+        roof = {"bound": w.bound, "achieved": round(kval, 2), "peak": round(peak, 1),
+                "unit": w.unit, "frac": round(kval / peak, 4), "peak_source": psrc,
+                "algorithmic": (f"{w.work:.6g} ops" if w.unit != "GB/s" else f"{w.bytes} bytes")}
+        if w.unit != "GB/s":
+            roof["frac_of_burst"] = round(kval / (peaks["bf16_tflops"] * mult), 4)
+            if peaks.get("bf16_tflops_sustained"):
+                roof["frac_of_sustained"] = round(
+                    kval / (peaks["bf16_tflops_sustained"] * mult), 4)
         out[key] = {"workload": w.name, "value": round(ws * kval, 2), "unit": w.unit,
                     "steps": steps, "ms_per_step": round(ms, 5),
                     "ms_per_step_eager": round(eager_ms, 5), "timing": how,
-                    "roofline": {"bound": w.bound, "achieved": round(kval, 2),
-                                 "peak": round(peak, 1), "unit": w.unit,
-                                 "frac": round(kval / peak, 4), "peak_source": psrc,
-                                 "algorithmic": (f"{w.work:.6g} ops" if w.unit != "GB/s"
-                                                 else f"{w.bytes} bytes")}}
+                    "roofline": roof, "clocks": clocks}
         del w
         torch.cuda.empty_cache()
     return out
