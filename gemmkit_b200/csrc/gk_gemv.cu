@@ -286,8 +286,9 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
     constexpr int CH = C::CH, NCH = C::NCH;
 
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~static_cast<uintptr_t>(1023));
+    // aligned by offsetting the shared array itself (not through an integer cast), so that
+    // every access through smem stays a shared-memory access for the compiler
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sW = smem;
     uint8_t* sX = smem + STAGES * C::W_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::RING_BYTES);

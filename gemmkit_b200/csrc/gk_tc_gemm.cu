@@ -75,8 +75,9 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
     constexpr int BKE = BKB / ES;  // K elements per stage
 
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~static_cast<uintptr_t>(1023));
+    // aligned by offsetting the shared array itself (not through an integer cast), so that
+    // every access through smem stays a shared-memory access for the compiler
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * C::A_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
