@@ -331,7 +331,8 @@ int gk_set_tile_n(int bn);
  * (`export GEMMKIT_CUDA_...=v`, the form the tuner's profile uses) and a process-wide run-time
  * override. gk_knob_names lists them (comma-separated): GEMMKIT_CUDA_BN (0 = per shape, or 16,
  * 32, 64, 128, 192, 256), GEMMKIT_CUDA_PAIR, GEMMKIT_CUDA_GEMV, GEMMKIT_CUDA_PDL,
- * GEMMKIT_CUDA_STREAMK, GEMMKIT_CUDA_GEMV_SK, GEMMKIT_CUDA_EPI16, GEMMKIT_CUDA_MN_B (0 / 1),
+ * GEMMKIT_CUDA_STREAMK, GEMMKIT_CUDA_GEMV_SK, GEMMKIT_CUDA_EPI16, GEMMKIT_CUDA_MN_B,
+ * GEMMKIT_CUDA_REQUANT_F32 (0 / 1),
  * GEMMKIT_CUDA_BN_SHORTK (as GEMMKIT_CUDA_BN), GEMMKIT_CUDA_STAGES (0 or 2 .. 12) and
  * GEMMKIT_CUDA_GEMV_SPLIT (0 .. 8). gk_knob_set with a negative value drops the run-time override;
  * an unknown name or an out-of-range value returns GK_EINVAL. */
