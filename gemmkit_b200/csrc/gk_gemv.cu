@@ -761,7 +761,7 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
         }
         cluster_sync();
         int qm = QM_GENERAL;
-        if (QUANT && warp >= 2 && rank == 0 && have) qm = pick_quant_mode(p.e, r_se);
+        if (QUANT && warp >= 2 && rank == 0 && have) qm = pick_quant_mode(s_epi, r_se);
         if (warp >= 2 && rank == 0 && have && grow < p.Mk) {
             for (int j = 1; j < p.split; ++j) {
                 const uint32_t* src = reinterpret_cast<const uint32_t*>(
@@ -781,7 +781,7 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
                 constexpr int QM = decltype(qm_tag)::value;
 #pragma unroll
                 for (int c = 0; c < NCH; ++c)
-                    epilogue_chunk<OUT, CH, QM>(v[c], p.Nk, p.e, grow * p.e.ldo, c * CH,
+                    epilogue_chunk<OUT, CH, QM>(v[c], p.Nk, s_epi, grow * s_epi.ldo, c * CH,
                                                 cp + c * CH, cbias + c * CH, r_se, r_nms, r_ulo,
                                                 r_uhi, r_bp, r_fb);
             });
@@ -789,7 +789,7 @@ __global__ void __launch_bounds__(192, GemvCfg<NB>::MIN_BLOCKS)
     }
 
     // mirrored outputs went to peer GPUs: make them visible system-wide before exiting
-    if (p.e.nmirror > 0 && warp >= 2) __threadfence_system();
+    if (s_epi.nmirror > 0 && warp >= 2) __threadfence_system();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, C::TMEM_COLS);

@@ -441,7 +441,7 @@ __global__ void __launch_bounds__(TileCfg<OUT, BN>::THREADS, 1)
     }
 
     // mirrored outputs went to peer GPUs: make them visible system-wide before exiting
-    if (p.e.nmirror > 0 && warp >= 2) __threadfence_system();
+    if (s_epi.nmirror > 0 && warp >= 2) __threadfence_system();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
