@@ -315,6 +315,7 @@ KNOBS = {
     "GEMMKIT_CUDA_GEMV_SPLIT": ([2, 4, 8], ("small_m",)),
     "GEMMKIT_CUDA_PDL": ([0, 1], ("small_m", "tile")),
     "GEMMKIT_CUDA_MN_B": ([0, 1], ("tile",)),
+    "GEMMKIT_CUDA_REQUANT_F32": ([0, 1], ("short_k",)),
 }
 
 

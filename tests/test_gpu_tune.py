@@ -103,7 +103,8 @@ def test_parity_under_tuned_profile():
     lines, and check a product of every shape class against the oracle; then restore."""
     before = {n: gk.knob_get(n) for n in gk.knob_names()}
     knobs = ("GEMMKIT_CUDA_BN,GEMMKIT_CUDA_BN_SHORTK,GEMMKIT_CUDA_EPI16,GEMMKIT_CUDA_STAGES,"
-             "GEMMKIT_CUDA_GEMV_SK,GEMMKIT_CUDA_GEMV_SPLIT,GEMMKIT_CUDA_MN_B")
+             "GEMMKIT_CUDA_GEMV_SK,GEMMKIT_CUDA_GEMV_SPLIT,GEMMKIT_CUDA_MN_B,"
+             "GEMMKIT_CUDA_REQUANT_F32")
     results, profile = tune.run(["--quick", "--dry-run", "--reps", "3", "--batch-ms", "2",
                                  "--knobs", knobs])
     exports = [ln.split()[1].split("=") for ln in profile.splitlines()
