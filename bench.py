@@ -608,10 +608,14 @@ def measure_single(args, ws, peaks) -> dict:
     back-to-back calls). Times are CUDA events, max over ranks."""
     import torch
     out = {}
+    # C3 last: its second of dense bf16 pulls the clocks down under the 1 kW cap, which would
+    # carry into a config timed right after it; each config starts after a short idle gap.
     specs = (("c1", C1, "CUDA-graph replay of 100 calls (eager calls are host-bound)"),
-             ("c3", C3, "eager, back to back"), ("c4", C4, "eager, back to back"))
+             ("c4", C4, "eager, back to back"), ("c3", C3, "eager, back to back"))
     for key, cls, how in specs:
         w = cls(7)
+        torch.cuda.synchronize()
+        time.sleep(0.5)
         steps = max(args.steps, 20)
         sampler = ClockSampler(torch.cuda.current_device(), 0.005) \
             if not torch.distributed.is_initialized() or torch.distributed.get_rank() == 0 \
@@ -971,9 +975,10 @@ def main():
         else:
             from gemmkit_b200.shard import ShardGroup
             grp = ShardGroup()
-            extra.update(measure_c3s(args, ws, grp, peaks))
-            torch.cuda.empty_cache()
+            # the epilogue-bound batch shard before the dense C3 routes (clocks, as above)
             extra.update(measure_c4s(args, ws, grp, peaks))
+            torch.cuda.empty_cache()
+            extra.update(measure_c3s(args, ws, grp, peaks))
             torch.cuda.empty_cache()
 
     cpu = None
